@@ -1,0 +1,173 @@
+/*
+ * pu_attn.h — C ABI of the B200 (sm_100a) attention library `libpu_attn.so`.
+ *
+ * This is the drop-in boundary for the attention hot path of Pallas-Unbound
+ * (a JAX/Pallas TPU project).  The reference exposes two jitted Python
+ * functions and no native ABI; each entry point below names the reference
+ * function (file:line inside the reference project) whose work it replaces.
+ * A JAX FFI handler, a ctypes stub or a torch op binds these symbols; the
+ * Python package `pallas_flash` in this repository is the ctypes binding.
+ *
+ * Conventions shared by every entry point
+ *   - Every tensor is a plain device pointer to a dense row-major array.
+ *     Attention tensors use the reference layout [B, H, N, D]
+ *     (src/pallas_flash/ops/interface.py:27, kernels/decoding.py:111).
+ *   - The caller owns every buffer.  No entry point allocates device memory
+ *     or synchronises the host; all work is enqueued on `stream`
+ *     (a cudaStream_t, NULL = legacy default stream).
+ *   - Return value: PU_OK (0) or a PU_ERR_* code; pu_last_error() gives a
+ *     human-readable message for the calling thread.
+ *   - Device-side waits are bounded.  A wait that runs out records
+ *     PU_ERR_DEVICE_TIMEOUT in a per-device status word that
+ *     pu_device_status() reads and clears.
+ *   - Thread-safe across devices; one stream per call.
+ */
+#ifndef PU_ATTN_H_
+#define PU_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PU_API __attribute__((visibility("default")))
+#else
+#define PU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define PU_OK 0
+#define PU_ERR_INVALID_ARGUMENT 1
+#define PU_ERR_UNSUPPORTED 2
+#define PU_ERR_CUDA 3
+#define PU_ERR_WORKSPACE 4
+#define PU_ERR_DEVICE_TIMEOUT 5
+
+/* element types */
+#define PU_DTYPE_BF16 0
+#define PU_DTYPE_F16 1
+#define PU_DTYPE_F32 2
+
+/* Number of floats in one packed split-KV partial record: m, l, o[D]. */
+#define PU_PARTIAL_FLOATS(D) ((D) + 2)
+
+/*
+ * Library identity: returns a static string with the build's target
+ * architecture and version.  No reference counterpart.
+ */
+PU_API const char* pu_version(void);
+
+/* Message for the last error raised on the calling thread ("" if none). */
+PU_API const char* pu_last_error(void);
+
+/*
+ * Synchronises the current device, then returns (and clears) its device
+ * status word: PU_OK, or PU_ERR_DEVICE_TIMEOUT when a kernel gave up on a
+ * bounded wait.  `*detail` (optional) receives the kernel's location code.
+ * No reference counterpart (the reference surfaces errors as XLA exceptions,
+ * tests/test_memory.py:59-69).
+ */
+PU_API int pu_device_status(int* detail);
+
+/*
+ * Training attention forward.
+ * Replaces pallas_flash_attention (src/pallas_flash/ops/interface.py:20-85),
+ * whose kernel is flash_attention_kernel (kernels/attention.py:11-36) running
+ * the online-softmax loop pipeline_kv_loop (kernels/pipeline.py:14-60).
+ *   q [B,H,Nq,D], k/v [B,H,Nkv,D], o [B,H,Nq,D]: bf16.
+ *   lse [B,H,Nq] fp32 natural-log LogSumExp of the scaled logits, or NULL.
+ *   D must be 64 or 128 (the host pads other head sizes, as the reference's
+ *   layout.pad_tensor does).  Any Nq, Nkv >= 1.
+ *   sm_scale multiplies q.k (the reference folds 1/sqrt(D) into q,
+ *   interface.py:43-44).  causal != 0 masks key j > query i (the causal
+ *   semantics of benchmarks/baseline_mha.py:47-50, top-left aligned).
+ */
+PU_API int pu_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                int64_t B, int64_t H, int64_t Nq, int64_t Nkv, int64_t D,
+                float sm_scale, int causal, void* stream);
+
+/*
+ * Bytes of device workspace pu_attn_bwd needs (an fp32 dQ accumulator and
+ * the row statistics Delta = rowsum(dO*O)).
+ */
+PU_API size_t pu_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t Nq, int64_t D);
+
+/*
+ * Training attention backward: dQ, dK, dV (bf16) from q, k, v, o, lse and dO.
+ * The reference has no backward kernel (forward only, no custom_vjp); this
+ * replaces the autodiff of benchmarks/baseline_mha.py:22-58.
+ *   workspace: >= pu_attn_bwd_workspace_size() bytes, 256-byte aligned;
+ *   its contents need not be initialised.
+ */
+PU_API int pu_attn_bwd(const void* q, const void* k, const void* v, const void* o,
+                const float* lse, const void* dout,
+                void* dq, void* dk, void* dv,
+                void* workspace, size_t workspace_bytes,
+                int64_t B, int64_t H, int64_t Nq, int64_t Nkv, int64_t D,
+                float sm_scale, int causal, void* stream);
+
+/*
+ * Bytes of device workspace the split-KV decode entry points need for a
+ * cache shard of n_local tokens.
+ */
+PU_API size_t pu_decode_workspace_size(int64_t B, int64_t H, int64_t n_local, int64_t D);
+
+/*
+ * Split-KV decode partial for one shard of the KV cache.
+ * Replaces decoding_kv_loop (src/pallas_flash/kernels/decoding.py:19-60),
+ * which returns (o, m, l) per (b, h); the reference discards m, l
+ * (decoding.py:73) — here they are the shard's output.
+ *   q [B,H,1,D] (q_dtype), k_cache/v_cache [B,H,n_local,D] (kv_dtype):
+ *   PU_DTYPE_F16 or PU_DTYPE_BF16.  D must be 128 or 64.
+ *   kv_lens: int32[B] device array of global sequence lengths, or NULL
+ *   (every sequence is kv_offset + n_local long).  Token t of this shard
+ *   has global position kv_offset + t and is masked when >= kv_lens[b]
+ *   (the padding mask of decoding.py:42-44).
+ *   partial: fp32 [B*H][D+2] records {m, l, o[D]}: m = max scaled logit
+ *   (natural-log units), l = sum exp(s - m), o = sum exp(s - m) v
+ *   (unnormalised).  An empty shard gives m = -inf, l = 0, o = 0.
+ *   workspace: >= pu_decode_workspace_size() bytes; it must be zero-filled
+ *   before its first use and is left zero-filled by every call that returns
+ *   PU_OK and completes on the device.
+ */
+PU_API int pu_decode_partial(const void* q, int q_dtype,
+                      const void* k_cache, const void* v_cache, int kv_dtype,
+                      const int32_t* kv_lens, int64_t kv_offset,
+                      float* partial, void* workspace, size_t workspace_bytes,
+                      int64_t B, int64_t H, int64_t n_local, int64_t D,
+                      float sm_scale, void* stream);
+
+/*
+ * Stable LogSumExp merge of G gathered shard partials into the attention
+ * output.  Replaces the documented-only psum merge of the reference
+ * (README.md:41-46, docs/project_plan.md:219-225); the algebra is the
+ * online-softmax update of kernels/pipeline.py:47-52 applied across shards.
+ *   partials: fp32 [G][B*H][D+2] (the layout an all-gather of
+ *   pu_decode_partial outputs produces).
+ *   o: bf16 [B,H,1,D] (the reference's output dtype, decoding.py:83-84).
+ *   lse: fp32 [B,H] natural-log LogSumExp, or NULL.
+ */
+PU_API int pu_decode_combine(const float* partials, int64_t G, void* o, float* lse,
+                      int64_t B, int64_t H, int64_t D, void* stream);
+
+/*
+ * Single-GPU decode step: pu_decode_partial over the whole cache with the
+ * merge fused into the same kernel (the last CTA of each (b, h) combines).
+ * Replaces pallas_flash_decoding (src/pallas_flash/kernels/decoding.py:105-145).
+ *   o bf16 [B,H,1,D]; lse fp32 [B,H] or NULL; workspace as above.
+ */
+PU_API int pu_decode(const void* q, int q_dtype,
+              const void* k_cache, const void* v_cache, int kv_dtype,
+              const int32_t* kv_lens, void* o, float* lse,
+              void* workspace, size_t workspace_bytes,
+              int64_t B, int64_t H, int64_t n, int64_t D,
+              float sm_scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PU_ATTN_H_ */

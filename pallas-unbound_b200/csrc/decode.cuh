@@ -1,0 +1,444 @@
+// decode.cuh — split-KV flash decode (one query token per (b, h)).
+//
+// Reference: decoding_kv_loop / flash_decoding_kernel
+// (src/pallas_flash/kernels/decoding.py:19-84) walk the whole cache of one
+// (b, h) in 128-token blocks with an online softmax and return (o, m, l).
+// Here the cache of each (b, h) is cut into `splits` contiguous chunks, one
+// CTA per chunk, so every SM streams K/V at once.  The kernel is HBM-bound:
+// each K/V row (D fp16/bf16 values) is read exactly once with 128-bit
+// streaming loads, D/8 lanes per row, 8 rows in flight per lane group.
+//
+// Per CTA: lane groups keep (m, l, o) in registers (log2 domain), merge
+// through shared memory, and write one split record to the workspace.  The
+// last CTA of each (b, h) (an atomic counter in the workspace, reset by that
+// CTA) merges the split records: into the bf16 output and LSE (single-GPU
+// step), or into the shard's packed partial {m, l, o[D]} that an NCCL
+// all-gather carries to the other ranks (sequence-sharded step).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "pu_host.cuh"
+#include "pu_ptx.cuh"
+
+namespace pu {
+namespace decode {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 8;        // rows in flight per lane group per iteration
+constexpr int kCtasPerSm = 2;     // occupancy the launch bounds ask for
+constexpr int kWaves = 4;         // CTAs per SM slot the split heuristic aims at
+constexpr int kMinChunk = 256;    // fewest tokens one CTA is given
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct Params {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* lens;   // [B] global lengths or nullptr
+  long long kv_offset;   // global position of local token 0
+  int n_local;           // tokens in this shard's cache
+  int H;
+  int splits;            // CTAs per (b, h)
+  int chunk;             // tokens per CTA (multiple of 16)
+  float scale_log2;      // sm_scale * log2(e)
+  float* ws_rec;         // [BH][splits][D+2] split records (log2-domain m)
+  int* ws_count;         // [BH] arrival counters (zero between calls)
+  // outputs
+  __nv_bfloat16* o;      // final mode: [BH][D]
+  float* lse;            // final mode: [BH] or nullptr
+  float* partial;        // partial mode: [BH][D+2] (natural-log m)
+};
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]);
+
+template <>
+__device__ __forceinline__ void unpack8<__half>(const uint4& w, float (&f)[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = *reinterpret_cast<const __half2*>(&u[i]);
+    float2 x = __half22float2(h);
+    f[2 * i] = x.x;
+    f[2 * i + 1] = x.y;
+  }
+}
+
+template <>
+__device__ __forceinline__ void unpack8<__nv_bfloat16>(const uint4& w, float (&f)[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // bf16 -> fp32 is a 16-bit shift
+    f[2 * i] = __uint_as_float(u[i] << 16);
+    f[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Merge (m, l, o[D]) records with a stable LogSumExp; m in log2 units.
+// Thread `d` (< D) produces column d.  Returns M and L through refs.
+template <int D>
+__device__ __forceinline__ void merge_records(const float* rec, int nrec, int stride, int d,
+                                              float& M, float& L, float& O) {
+  M = -INFINITY;
+  for (int g = 0; g < nrec; ++g) M = fmaxf(M, __ldcg(rec + (size_t)g * stride));
+  L = 0.f;
+  O = 0.f;
+  if (M == -INFINITY) return;
+  for (int g = 0; g < nrec; ++g) {
+    const float* r = rec + (size_t)g * stride;
+    const float mg = __ldcg(r);
+    if (mg == -INFINITY) continue;
+    const float w = ex2(mg - M);
+    L += w * __ldcg(r + 1);
+    O += w * __ldcg(r + 2 + d);
+  }
+}
+
+template <typename QT, typename KVT, int D, bool kFinal>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Params p) {
+  constexpr int LPR = D / 8;        // lanes per cache row
+  constexpr int RPW = 32 / LPR;     // rows per warp instruction
+  constexpr int ROWS_PER_ITER = kWarps * RPW * kUnroll;
+  constexpr int NGROUP = kWarps * RPW;  // lane groups per CTA
+  static_assert(D == 64 || D == 128, "head size");
+
+  __shared__ float sm_m[NGROUP];
+  __shared__ float sm_l[NGROUP];
+  __shared__ float sm_o[NGROUP][D];
+  __shared__ int sm_last;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int sub = lane % LPR;       // which 8 columns of the row
+  const int rw = lane / LPR;        // which row of the warp instruction
+  const int split = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H;
+
+  int len = p.n_local;
+  if (p.lens != nullptr) {
+    long long g = (long long)p.lens[b] - p.kv_offset;
+    len = g < 0 ? 0 : (g > p.n_local ? p.n_local : (int)g);
+  }
+  const int t_begin = split * p.chunk;
+  const int t_end = min(t_begin + p.chunk, len);
+
+  // query slice, pre-scaled into log2 units
+  float qf[8];
+  {
+    const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const QT*>(p.q) + (size_t)bh * D + sub * 8);
+    unpack8<QT>(w, qf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qf[i] *= p.scale_log2;
+  }
+
+  const KVT* kb = static_cast<const KVT*>(p.k) + (size_t)bh * p.n_local * D + sub * 8;
+  const KVT* vb = static_cast<const KVT*>(p.v) + (size_t)bh * p.n_local * D + sub * 8;
+
+  float m = -INFINITY, l = 0.f;
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = 0.f;
+
+  for (int base = t_begin + warp * RPW * kUnroll; base < t_end; base += ROWS_PER_ITER) {
+    uint4 kw[kUnroll], vw[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int t = base + u * RPW + rw;
+      if (t < t_end) {
+        kw[u] = ld_stream(reinterpret_cast<const uint4*>(kb + (size_t)t * D));
+        vw[u] = ld_stream(reinterpret_cast<const uint4*>(vb + (size_t)t * D));
+      } else {
+        kw[u] = make_uint4(0, 0, 0, 0);
+        vw[u] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    float s[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      float kf[8];
+      unpack8<KVT>(kw[u], kf);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = fmaf(qf[i], kf[i], acc);
+      s[u] = acc;
+    }
+#pragma unroll
+    for (int off = LPR / 2; off > 0; off >>= 1) {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], off);
+    }
+    float gmax = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int t = base + u * RPW + rw;
+      if (t >= t_end) s[u] = -INFINITY;
+      gmax = fmaxf(gmax, s[u]);
+    }
+    const float m_new = fmaxf(m, gmax);
+    if (m_new == -INFINITY) continue;  // nothing valid yet in this lane group
+    const float alpha = ex2(m - m_new);
+    l *= alpha;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] *= alpha;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const float pu_ = ex2(s[u] - m_new);
+      l += pu_;
+      float vf[8];
+      unpack8<KVT>(vw[u], vf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = fmaf(pu_, vf[i], o[i]);
+    }
+    m = m_new;
+  }
+
+  // merge the lane groups of this CTA
+  const int grp = warp * RPW + rw;
+  if (sub == 0) {
+    sm_m[grp] = m;
+    sm_l[grp] = l;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sm_o[grp][sub * 8 + i] = o[i];
+  __syncthreads();
+
+  float* rec = p.ws_rec + ((size_t)bh * p.splits + split) * (D + 2);
+  if (tid < D) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < NGROUP; ++g) M = fmaxf(M, sm_m[g]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int g = 0; g < NGROUP; ++g) {
+        const float w = (sm_m[g] == -INFINITY) ? 0.f : ex2(sm_m[g] - M);
+        L += w * sm_l[g];
+        O += w * sm_o[g][tid];
+      }
+    }
+    rec[2 + tid] = O;
+    if (tid == 0) {
+      rec[0] = M;
+      rec[1] = L;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(p.ws_count + bh, 1);
+    sm_last = (prev == p.splits - 1);
+  }
+  __syncthreads();
+  if (!sm_last) return;
+  __threadfence();
+
+  // last CTA of this (b, h): merge every split record
+  if (tid < D) {
+    float M, L, O;
+    merge_records<D>(p.ws_rec + (size_t)bh * p.splits * (D + 2), p.splits, D + 2, tid, M, L, O);
+    if constexpr (kFinal) {
+      const float out = (L > 0.f) ? O / L : 0.f;
+      p.o[(size_t)bh * D + tid] = __float2bfloat16_rn(out);
+      if (tid == 0 && p.lse != nullptr) {
+        p.lse[bh] = (L > 0.f) ? (M + lg2(L)) * kLn2 : -INFINITY;
+      }
+    } else {
+      float* out = p.partial + (size_t)bh * (D + 2);
+      out[2 + tid] = O;
+      if (tid == 0) {
+        out[0] = (M == -INFINITY) ? -INFINITY : M * kLn2;
+        out[1] = L;
+      }
+    }
+  }
+  if (tid == 0) p.ws_count[bh] = 0;  // leave the workspace zeroed for the next call
+}
+
+// Merge G gathered shard records {m (natural log), l, o[D]} per (b, h).
+template <int D>
+__global__ void __launch_bounds__(D) combine_kernel(const float* __restrict__ parts, int G, int BH,
+                                                    __nv_bfloat16* __restrict__ o,
+                                                    float* __restrict__ lse) {
+  const int bh = blockIdx.x;
+  const int d = threadIdx.x;
+  const size_t stride = (size_t)BH * (D + 2);
+  float M = -INFINITY;
+  for (int g = 0; g < G; ++g) M = fmaxf(M, parts[g * stride + (size_t)bh * (D + 2)]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+    for (int g = 0; g < G; ++g) {
+      const float* r = parts + g * stride + (size_t)bh * (D + 2);
+      if (r[0] == -INFINITY) continue;
+      const float w = ex2((r[0] - M) * kLog2e);
+      L += w * r[1];
+      O += w * r[2 + d];
+    }
+  }
+  o[(size_t)bh * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+  if (d == 0 && lse != nullptr) lse[bh] = (L > 0.f) ? M + logf(L) : -INFINITY;
+}
+
+struct Plan {
+  int splits;
+  int chunk;
+  size_t rec_bytes;    // split records
+  size_t count_off;    // byte offset of the counters
+  size_t total_bytes;
+};
+
+inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms) {
+  Plan pl{};
+  const long long target = (long long)num_sms * kCtasPerSm * kWaves;
+  long long splits = (target + BH - 1) / BH;
+  const long long max_splits = std::max<long long>(1, (n_local + kMinChunk - 1) / kMinChunk);
+  splits = std::max<long long>(1, std::min(splits, max_splits));
+  long long chunk = (n_local + splits - 1) / splits;
+  chunk = std::max<long long>(16, (chunk + 15) / 16 * 16);
+  splits = std::max<long long>(1, (n_local + chunk - 1) / chunk);
+  pl.splits = (int)splits;
+  pl.chunk = (int)chunk;
+  pl.rec_bytes = round_up((size_t)BH * splits * (D + 2) * sizeof(float), 256);
+  pl.count_off = pl.rec_bytes;
+  pl.total_bytes = pl.count_off + round_up((size_t)BH * sizeof(int), 256);
+  return pl;
+}
+
+template <bool kFinal>
+int launch(const Params& prm, int q_dtype, int kv_dtype, int D, int BH, cudaStream_t st) {
+  dim3 grid(prm.splits, BH);
+  dim3 block(kThreads);
+#define PU_DECODE_LAUNCH(QT, KVT, DD) split_kv_kernel<QT, KVT, DD, kFinal><<<grid, block, 0, st>>>(prm)
+  const bool qh = (q_dtype == PU_DTYPE_F16);
+  const bool kh = (kv_dtype == PU_DTYPE_F16);
+  if (D == 128) {
+    if (qh && kh) PU_DECODE_LAUNCH(__half, __half, 128);
+    else if (qh && !kh) PU_DECODE_LAUNCH(__half, __nv_bfloat16, 128);
+    else if (!qh && kh) PU_DECODE_LAUNCH(__nv_bfloat16, __half, 128);
+    else PU_DECODE_LAUNCH(__nv_bfloat16, __nv_bfloat16, 128);
+  } else {
+    if (qh && kh) PU_DECODE_LAUNCH(__half, __half, 64);
+    else if (qh && !kh) PU_DECODE_LAUNCH(__half, __nv_bfloat16, 64);
+    else if (!qh && kh) PU_DECODE_LAUNCH(__nv_bfloat16, __half, 64);
+    else PU_DECODE_LAUNCH(__nv_bfloat16, __nv_bfloat16, 64);
+  }
+#undef PU_DECODE_LAUNCH
+  return check_cuda(cudaGetLastError(), "split-KV decode launch");
+}
+
+inline int check_args(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype,
+                      long long B, long long H, long long n, long long D) {
+  if (!q || !k || !v) return set_error(PU_ERR_INVALID_ARGUMENT, "null q/k/v pointer");
+  if (B <= 0 || H <= 0 || n <= 0) return set_error(PU_ERR_INVALID_ARGUMENT, "B, H and the cache length must be positive");
+  if (D != 128 && D != 64) return set_error(PU_ERR_UNSUPPORTED, "decode head size %lld (supported: 64, 128)", D);
+  if ((q_dtype != PU_DTYPE_F16 && q_dtype != PU_DTYPE_BF16) ||
+      (kv_dtype != PU_DTYPE_F16 && kv_dtype != PU_DTYPE_BF16))
+    return set_error(PU_ERR_UNSUPPORTED, "decode dtypes must be f16 or bf16");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v))
+    return set_error(PU_ERR_INVALID_ARGUMENT, "q/k/v must be 16-byte aligned");
+  if (B * H > 65535) return set_error(PU_ERR_UNSUPPORTED, "B*H = %lld exceeds 65535", B * H);
+  if (n > (1ll << 30)) return set_error(PU_ERR_UNSUPPORTED, "cache length too large");
+  return PU_OK;
+}
+
+}  // namespace decode
+}  // namespace pu
+
+extern "C" {
+
+size_t pu_decode_workspace_size(int64_t B, int64_t H, int64_t n_local, int64_t D) {
+  if (B <= 0 || H <= 0 || n_local <= 0 || D <= 0) return 0;
+  return pu::decode::make_plan(B * H, n_local, D, pu::sm_count()).total_bytes;
+}
+
+int pu_decode_partial(const void* q, int q_dtype, const void* k_cache, const void* v_cache,
+                      int kv_dtype, const int32_t* kv_lens, int64_t kv_offset, float* partial,
+                      void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                      int64_t n_local, int64_t D, float sm_scale, void* stream) {
+  using namespace pu::decode;
+  int rc = check_args(q, q_dtype, k_cache, v_cache, kv_dtype, B, H, n_local, D);
+  if (rc) return rc;
+  if (!partial) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null partial output");
+  if (kv_offset < 0) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "negative kv_offset");
+  const Plan pl = make_plan(B * H, n_local, D, pu::sm_count());
+  if (!workspace || workspace_bytes < pl.total_bytes)
+    return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
+                         workspace_bytes);
+  Params prm{};
+  prm.q = q;
+  prm.k = k_cache;
+  prm.v = v_cache;
+  prm.lens = kv_lens;
+  prm.kv_offset = kv_offset;
+  prm.n_local = (int)n_local;
+  prm.H = (int)H;
+  prm.splits = pl.splits;
+  prm.chunk = pl.chunk;
+  prm.scale_log2 = sm_scale * kLog2e;
+  prm.ws_rec = static_cast<float*>(workspace);
+  prm.ws_count = reinterpret_cast<int*>(static_cast<char*>(workspace) + pl.count_off);
+  prm.partial = partial;
+  return launch<false>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));
+}
+
+int pu_decode(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
+              const int32_t* kv_lens, void* o, float* lse, void* workspace, size_t workspace_bytes,
+              int64_t B, int64_t H, int64_t n, int64_t D, float sm_scale, void* stream) {
+  using namespace pu::decode;
+  int rc = check_args(q, q_dtype, k_cache, v_cache, kv_dtype, B, H, n, D);
+  if (rc) return rc;
+  if (!o) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null output");
+  const Plan pl = make_plan(B * H, n, D, pu::sm_count());
+  if (!workspace || workspace_bytes < pl.total_bytes)
+    return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
+                         workspace_bytes);
+  Params prm{};
+  prm.q = q;
+  prm.k = k_cache;
+  prm.v = v_cache;
+  prm.lens = kv_lens;
+  prm.kv_offset = 0;
+  prm.n_local = (int)n;
+  prm.H = (int)H;
+  prm.splits = pl.splits;
+  prm.chunk = pl.chunk;
+  prm.scale_log2 = sm_scale * kLog2e;
+  prm.ws_rec = static_cast<float*>(workspace);
+  prm.ws_count = reinterpret_cast<int*>(static_cast<char*>(workspace) + pl.count_off);
+  prm.o = static_cast<__nv_bfloat16*>(o);
+  prm.lse = lse;
+  return launch<true>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));
+}
+
+int pu_decode_combine(const float* partials, int64_t G, void* o, float* lse, int64_t B, int64_t H,
+                      int64_t D, void* stream) {
+  using namespace pu::decode;
+  if (!partials || !o) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null partials/output");
+  if (G <= 0 || B <= 0 || H <= 0) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "G, B, H must be positive");
+  if (D != 128 && D != 64) return pu::set_error(PU_ERR_UNSUPPORTED, "combine head size %lld", (long long)D);
+  const int BH = (int)(B * H);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 128)
+    combine_kernel<128><<<BH, 128, 0, st>>>(partials, (int)G, BH, static_cast<__nv_bfloat16*>(o), lse);
+  else
+    combine_kernel<64><<<BH, 64, 0, st>>>(partials, (int)G, BH, static_cast<__nv_bfloat16*>(o), lse);
+  return pu::check_cuda(cudaGetLastError(), "decode combine launch");
+}
+
+}  // extern "C"

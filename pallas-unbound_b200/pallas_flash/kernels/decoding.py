@@ -1,0 +1,147 @@
+"""Decode entry point — drop-in for the reference's
+`pallas_flash.kernels.decoding.pallas_flash_decoding`
+(src/pallas_flash/kernels/decoding.py:105-145).
+
+`pallas_flash_decoding(q, k_cache, v_cache)`: q [B,H,1,D], caches
+[B,H,N,D]; returns bf16 [B,H,1,D] (the reference's output dtype).  The
+reference casts every input to bf16 first (decoding.py:107-109); here fp16
+and bf16 caches are read as they are (same bytes, no cast pass), other
+dtypes are cast to bf16.
+
+Keyword-only additions:
+  kv_lens     int32 [B] per-sequence lengths (positions >= length masked,
+              the reference's padding mask decoding.py:42-44 made ragged)
+  sm_scale    default 1/sqrt(D)
+  return_lse  also return fp32 LSE [B,H]
+  group       a torch.distributed process group over which the cache is
+              sharded by SEQUENCE: rank r holds tokens
+              [r*N_local, (r+1)*N_local) of every sequence.  Each rank runs
+              the split-KV kernel on its shard, the packed (m, l, o)
+              partials are all-gathered over NCCL, and a fused stable-LSE
+              kernel merges them (the split-KV scheme the reference documents,
+              README.md:41-46, but never implements).
+"""
+from __future__ import annotations
+
+import math
+import threading
+from typing import Optional
+
+import torch
+
+from .. import _lib
+
+__all__ = ["pallas_flash_decoding", "decode_partial", "decode_combine", "DecodeWorkspace"]
+
+_DT = {torch.float16: _lib.PU_DTYPE_F16, torch.bfloat16: _lib.PU_DTYPE_BF16}
+
+
+class DecodeWorkspace:
+    """Zero-initialised device scratch for the split-KV kernels, cached per
+    (device, stream).  The kernels leave it zeroed after each call, so one
+    workspace must not be shared by decode calls that overlap on the GPU."""
+
+    _cache: dict = {}
+    _lock = threading.Lock()
+
+    @classmethod
+    def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
+        stream = torch.cuda.current_stream(device).cuda_stream
+        key = (device.index, stream)
+        with cls._lock:
+            buf = cls._cache.get(key)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+                cls._cache[key] = buf
+            return buf
+
+
+def _prep(t: torch.Tensor, dev: torch.device) -> torch.Tensor:
+    t = t.to(dev, non_blocking=True)
+    if t.dtype not in _DT:
+        t = t.to(torch.bfloat16)
+    return t.contiguous()
+
+
+def decode_partial(q, k_cache, v_cache, *, kv_offset: int = 0, kv_lens=None,
+                   sm_scale: Optional[float] = None, out: Optional[torch.Tensor] = None):
+    """Packed shard partial fp32 [B*H, D+2] = {m, l, o[D]} (pu_decode_partial)."""
+    B, H, _, D = q.shape
+    n_local = k_cache.shape[2]
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B * H, D + 2), dtype=torch.float32, device=q.device)
+    lib = _lib.lib()
+    need = int(lib.pu_decode_workspace_size(B, H, n_local, D))
+    ws = DecodeWorkspace.get(q.device, need)
+    lens_ptr = kv_lens.data_ptr() if kv_lens is not None else None
+    _lib.check(lib.pu_decode_partial(q.data_ptr(), _DT[q.dtype], k_cache.data_ptr(),
+                                     v_cache.data_ptr(), _DT[k_cache.dtype], lens_ptr,
+                                     int(kv_offset), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                     B, H, n_local, D, float(sm_scale),
+                                     torch.cuda.current_stream().cuda_stream),
+               "pu_decode_partial")
+    return out
+
+
+def decode_combine(parts: torch.Tensor, B: int, H: int, D: int, *, out=None, lse=None):
+    """Merge gathered partials fp32 [G, B*H, D+2] -> (o bf16 [B,H,1,D], lse fp32 [B,H])."""
+    G = parts.shape[0]
+    if out is None:
+        out = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device=parts.device)
+    if lse is None:
+        lse = torch.empty((B, H), dtype=torch.float32, device=parts.device)
+    _lib.check(_lib.lib().pu_decode_combine(parts.data_ptr(), G, out.data_ptr(), lse.data_ptr(),
+                                            B, H, D, torch.cuda.current_stream().cuda_stream),
+               "pu_decode_combine")
+    return out, lse
+
+
+def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+                          kv_lens: Optional[torch.Tensor] = None,
+                          sm_scale: Optional[float] = None, return_lse: bool = False,
+                          group=None):
+    """One decode step of attention for a query token per (b, h)."""
+    if q.dim() != 4 or q.shape[2] != 1:
+        raise ValueError("q must be [B, H, 1, D]")
+    if k_cache.shape != v_cache.shape or k_cache.shape[:2] != q.shape[:2] \
+            or k_cache.shape[3] != q.shape[3]:
+        raise ValueError(f"cache shape {tuple(k_cache.shape)} does not match q {tuple(q.shape)}")
+    host = not q.is_cuda
+    dev = torch.device("cuda", torch.cuda.current_device()) if host else q.device
+    q_, k_, v_ = _prep(q, dev), _prep(k_cache, dev), _prep(v_cache, dev)
+    B, H, _, D = q_.shape
+    if D not in (64, 128):
+        raise ValueError(f"decode head size {D} (supported: 64, 128)")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    lens = None
+    if kv_lens is not None:
+        lens = torch.as_tensor(kv_lens, dtype=torch.int32).to(dev, non_blocking=True).contiguous()
+        if lens.numel() != B:
+            raise ValueError("kv_lens must have B entries")
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    n_local = k_.shape[2]
+    if group is None:
+        o = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device=dev)
+        lse = torch.empty((B, H), dtype=torch.float32, device=dev)
+        need = int(lib.pu_decode_workspace_size(B, H, n_local, D))
+        ws = DecodeWorkspace.get(dev, need)
+        _lib.check(lib.pu_decode(q_.data_ptr(), _DT[q_.dtype], k_.data_ptr(), v_.data_ptr(),
+                                 _DT[k_.dtype], lens.data_ptr() if lens is not None else None,
+                                 o.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), B, H,
+                                 n_local, D, float(sm_scale), stream), "pu_decode")
+    else:
+        from ..distributed.collectives import all_gather_partials
+        import torch.distributed as dist
+        rank = dist.get_rank(group)
+        world = dist.get_world_size(group)
+        part = decode_partial(q_, k_, v_, kv_offset=rank * n_local, kv_lens=lens,
+                              sm_scale=sm_scale)
+        gathered = all_gather_partials(part, world, group)
+        o, lse = decode_combine(gathered, B, H, D)
+    if host:
+        o, lse = o.cpu(), lse.cpu()
+    return (o, lse) if return_lse else o

@@ -1,0 +1,149 @@
+"""Training attention entry point — drop-in for the reference's
+`pallas_flash.ops.interface.pallas_flash_attention`
+(src/pallas_flash/ops/interface.py:20-85).
+
+Same name and positional signature: `pallas_flash_attention(q, k, v)` takes
+[B, H, N, D] tensors of any float dtype, casts them to bf16
+(interface.py:23-25) and returns bf16 `o` shaped like q.  Keyword-only
+additions (defaults keep the reference's behaviour): `causal`,
+`sm_scale` (default 1/sqrt(D)), `return_lse`.  It is differentiable: the
+backward pass (which the reference lacks) reuses the saved LSE.
+
+Inputs may live on the GPU (the usual case) or on the host; host tensors are
+copied to the current CUDA device and the results copied back.  Every
+compute step runs in libpu_attn.so (sm_100a); there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from .. import _lib
+from ..kernels.layout import kernel_head_dim, pad_head_dim
+
+__all__ = ["pallas_flash_attention", "flash_attention_forward", "flash_attention_backward",
+           "bwd_workspace_bytes"]
+
+
+def _stream_handle() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+
+
+def flash_attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                            causal: bool = False, sm_scale: Optional[float] = None,
+                            out: Optional[torch.Tensor] = None,
+                            lse: Optional[torch.Tensor] = None):
+    """Low-level forward on CUDA bf16 tensors with D in {64, 128}.
+
+    Returns (o bf16 [B,H,Nq,D], lse fp32 [B,H,Nq]).  `out`/`lse` may be
+    preallocated.  Calls pu_attn_fwd on the current stream.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(t, name)
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{name} must be bf16")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, H, Nq, D = q.shape
+    Nkv = k.shape[2]
+    if k.shape != (B, H, Nkv, D) or v.shape != k.shape:
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((B, H, Nq), dtype=torch.float32, device=q.device)
+    _lib.check(_lib.lib().pu_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                      lse.data_ptr(), B, H, Nq, Nkv, D, float(sm_scale),
+                                      int(bool(causal)), _stream_handle()), "pu_attn_fwd")
+    return out, lse
+
+
+def bwd_workspace_bytes(B: int, H: int, Nq: int, D: int) -> int:
+    return int(_lib.lib().pu_attn_bwd_workspace_size(B, H, Nq, D))
+
+
+def flash_attention_backward(q, k, v, o, lse, do, *, causal: bool = False,
+                             sm_scale: Optional[float] = None,
+                             workspace: Optional[torch.Tensor] = None,
+                             dq: Optional[torch.Tensor] = None,
+                             dk: Optional[torch.Tensor] = None,
+                             dv: Optional[torch.Tensor] = None):
+    """Low-level backward on CUDA bf16 tensors; returns (dq, dk, dv) bf16."""
+    for name, t in (("q", q), ("k", k), ("v", v), ("o", o), ("do", do)):
+        _require_cuda(t, name)
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{name} must be bf16")
+    q, k, v, o, do = (t.contiguous() for t in (q, k, v, o, do))
+    lse = lse.contiguous()
+    B, H, Nq, D = q.shape
+    Nkv = k.shape[2]
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    need = bwd_workspace_bytes(B, H, Nq, D)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
+    _lib.check(_lib.lib().pu_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                      lse.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                      dv.data_ptr(), workspace.data_ptr(), need, B, H, Nq, Nkv, D,
+                                      float(sm_scale), int(bool(causal)), _stream_handle()),
+               "pu_attn_bwd")
+    return dq, dk, dv
+
+
+class _FlashAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, sm_scale):
+        o, lse = flash_attention_forward(q, k, v, causal=causal, sm_scale=sm_scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.causal = causal
+        ctx.sm_scale = sm_scale
+        ctx.mark_non_differentiable(lse)
+        return o, lse
+
+    @staticmethod
+    def backward(ctx, do, _dlse):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = flash_attention_backward(q, k, v, o, lse, do.to(torch.bfloat16),
+                                              causal=ctx.causal, sm_scale=ctx.sm_scale)
+        return dq, dk, dv, None, None
+
+
+def pallas_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                           causal: bool = False, sm_scale: Optional[float] = None,
+                           return_lse: bool = False):
+    """softmax(q k^T * sm_scale [+ causal mask]) v on the B200 kernels.
+
+    q [B,H,Nq,D], k/v [B,H,Nkv,D] of any float dtype (cast to bf16, as the
+    reference does).  Returns bf16 o shaped like q, or (o, lse) when
+    `return_lse`.  Head sizes other than 64/128 are zero-padded for the
+    kernel and sliced back (the reference's pad/unpad, layout.py); the scale
+    defaults to 1/sqrt(D) of the true head size.
+    """
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("q, k, v must be [B, H, N, D]")
+    host = not q.is_cuda
+    dev = torch.device("cuda", torch.cuda.current_device()) if host else q.device
+    q_, k_, v_ = (t.to(device=dev, dtype=torch.bfloat16, non_blocking=True) for t in (q, k, v))
+    D = q.shape[-1]
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    Dk = kernel_head_dim(D)
+    q_, k_, v_ = (pad_head_dim(t, Dk) for t in (q_, k_, v_))
+    o, lse = _FlashAttention.apply(q_, k_, v_, bool(causal), float(sm_scale))
+    if Dk != D:
+        o = o[..., :D]
+    if host:
+        o = o.to("cpu")
+        lse = lse.to("cpu")
+    return (o, lse) if return_lse else o

@@ -1,0 +1,58 @@
+"""The C-ABI library builds for sm_100a, loads on a host without a GPU, and
+exports every entry point declared in include/pu_attn.h (no compute calls)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols() -> list[str]:
+    text = (ROOT / "include" / "pu_attn.h").read_text()
+    return re.findall(r"PU_API\s+[\w\s\*]+?\b(pu_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for required in ("pu_attn_fwd", "pu_attn_bwd", "pu_decode", "pu_decode_partial",
+                     "pu_decode_combine", "pu_last_error", "pu_device_status"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    lib = ctypes.CDLL(str(built_lib))
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, f"missing exports: {missing}"
+
+
+def test_python_binding_matches_header(built_lib):
+    from pallas_flash import _lib
+    assert set(_lib.SIGNATURES) == set(declared_symbols())
+    handle = _lib.lib()
+    assert b"sm_100a" in handle.pu_version()
+
+
+def test_library_is_sm100a_only(built_lib):
+    """The build targets sm_100a exclusively (no PTX for other archs)."""
+    import subprocess
+    out = subprocess.run(["cuobjdump", "--list-elf", str(built_lib)], capture_output=True,
+                         text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    archs = set(re.findall(r"sm_(\d+a?)", out.stdout))
+    assert archs == {"100a"}, archs
+
+
+def test_argument_errors_are_reported_without_gpu(built_lib):
+    """Bad arguments are rejected on the host before any CUDA call."""
+    from pallas_flash import _lib
+    lib = _lib.lib()
+    rc = lib.pu_attn_fwd(None, None, None, None, None, 1, 1, 1, 1, 128, 0.1, 0, None)
+    assert rc == _lib.PU_ERR_INVALID_ARGUMENT
+    assert b"null" in lib.pu_last_error()
+    rc = lib.pu_decode_combine(None, 1, None, None, 1, 1, 128, None)
+    assert rc == _lib.PU_ERR_INVALID_ARGUMENT
