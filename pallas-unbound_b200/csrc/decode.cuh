@@ -293,11 +293,16 @@ __global__ void __launch_bounds__(D) combine_kernel(const float* __restrict__ pa
   if (d == 0 && lse != nullptr) lse[bh] = (L > 0.f) ? M + logf(L) : -INFINITY;
 }
 
+// Workspace layout: [0, kCountBytes) arrival counters, one int per (b, h),
+// at a fixed place so that calls of different shapes sharing one workspace
+// never see another call's split records as counters; then the records.
+constexpr int kMaxBH = 65535;
+constexpr size_t kCountBytes = 256 * 1024;  // >= kMaxBH * sizeof(int), 256-aligned
+
 struct Plan {
   int splits;
   int chunk;
-  size_t rec_bytes;    // split records
-  size_t count_off;    // byte offset of the counters
+  size_t rec_off;      // byte offset of the split records
   size_t total_bytes;
 };
 
@@ -314,9 +319,8 @@ inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms)
   splits = std::max<long long>(1, (n_local + chunk - 1) / chunk);
   pl.splits = (int)splits;
   pl.chunk = (int)chunk;
-  pl.rec_bytes = round_up((size_t)BH * splits * (D + 2) * sizeof(float), 256);
-  pl.count_off = pl.rec_bytes;
-  pl.total_bytes = pl.count_off + round_up((size_t)BH * sizeof(int), 256);
+  pl.rec_off = kCountBytes;
+  pl.total_bytes = pl.rec_off + round_up((size_t)BH * splits * (D + 2) * sizeof(float), 256);
   return pl;
 }
 
@@ -352,7 +356,7 @@ inline int check_args(const void* q, int q_dtype, const void* k, const void* v, 
     return set_error(PU_ERR_UNSUPPORTED, "decode dtypes must be f16 or bf16");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v))
     return set_error(PU_ERR_INVALID_ARGUMENT, "q/k/v must be 16-byte aligned");
-  if (B * H > 65535) return set_error(PU_ERR_UNSUPPORTED, "B*H = %lld exceeds 65535", B * H);
+  if (B * H > kMaxBH) return set_error(PU_ERR_UNSUPPORTED, "B*H = %lld exceeds %d", B * H, kMaxBH);
   if (n > (1ll << 30)) return set_error(PU_ERR_UNSUPPORTED, "cache length too large");
   return PU_OK;
 }
@@ -391,8 +395,8 @@ int pu_decode_partial(const void* q, int q_dtype, const void* k_cache, const voi
   prm.splits = pl.splits;
   prm.chunk = pl.chunk;
   prm.scale_log2 = sm_scale * kLog2e;
-  prm.ws_rec = static_cast<float*>(workspace);
-  prm.ws_count = reinterpret_cast<int*>(static_cast<char*>(workspace) + pl.count_off);
+  prm.ws_rec = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.rec_off);
+  prm.ws_count = static_cast<int*>(workspace);
   prm.partial = partial;
   return launch<false>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));
 }
@@ -419,8 +423,8 @@ int pu_decode(const void* q, int q_dtype, const void* k_cache, const void* v_cac
   prm.splits = pl.splits;
   prm.chunk = pl.chunk;
   prm.scale_log2 = sm_scale * kLog2e;
-  prm.ws_rec = static_cast<float*>(workspace);
-  prm.ws_count = reinterpret_cast<int*>(static_cast<char*>(workspace) + pl.count_off);
+  prm.ws_rec = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.rec_off);
+  prm.ws_count = static_cast<int*>(workspace);
   prm.o = static_cast<__nv_bfloat16*>(o);
   prm.lse = lse;
   return launch<true>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));
