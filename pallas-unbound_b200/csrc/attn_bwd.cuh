@@ -1,14 +1,593 @@
-// attn_bwd.cuh — training-attention backward (placeholder until the tcgen05
-// kernel lands).
+// attn_bwd.cuh — training-attention backward on tcgen05 tensor cores.
+//
+// The reference has no backward kernel (its Pallas kernel is forward-only and
+// discards m, l; src/pallas_flash/kernels/attention.py:25).  This computes the
+// gradients of the attention of benchmarks/baseline_mha.py:22-58 from the
+// forward's saved LSE:
+//   P = exp(scale*Q K^T - LSE),  dV = P^T dO,  dP = dO V^T,
+//   Delta = rowsum(dO * O),      dS = P * (dP - Delta),
+//   dQ = scale * dS K,           dK = scale * dS^T Q.
+//
+// Three kernels:
+//   prep   : Delta[b,h,i] (fp32) and zeroing of the fp32 dQ accumulator.
+//   main   : one CTA per 128-row K/V tile of one (b, h); K and V stay in
+//            shared memory while 128-row Q / dO tiles stream through a
+//            2-deep TMA ring.  Per query tile (transposed formulation, TMEM
+//            lanes = key rows):
+//              S^T  = K Q^T      -> TMEM [0,128)
+//              dP^T = V dO^T     -> TMEM [128,256)
+//              softmax warps: P^T = exp2(S^T*scale*log2e - LSE*log2e) (bf16,
+//                into shared memory), then dS^T = P^T (dP^T - Delta)
+//              dV  += P^T dO     -> TMEM [256,256+D)
+//              dK  += dS^T Q     -> TMEM [384,384+D)
+//              dQ_i = dS K       -> TMEM [0,D) (reuses S^T's columns), drained
+//                                   by the softmax warps into the fp32 dQ
+//                                   accumulator with vector reductions.
+//            P^T and dS^T share one shared-memory tile (dS^T is written once
+//            the dV product has consumed P^T).
+//   post   : dQ = bf16(scale * dQ accumulator).
+// Warp roles of the main kernel as in the forward: warps 0-3 softmax/drain,
+// warp 4 TMA producer, warp 5 tcgen05 issuer + TMEM owner.
 #pragma once
-#include "pu_host.cuh"
 
-extern "C" size_t pu_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t Nq, int64_t D) {
-  return (size_t)(B * H * Nq * D * 4 + B * H * Nq * 4 + 4096);
+#include <cuda_bf16.h>
+
+#include "pu_host.cuh"
+#include "pu_ptx.cuh"
+
+namespace pu {
+namespace bwd {
+
+constexpr int BM = 128;   // query rows per streamed tile
+constexpr int BN = 128;   // key/value rows per CTA
+constexpr int kThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
+
+template <int D>
+struct Cfg {
+  static constexpr int NSQ = 2;                  // Q / dO ring depth
+  static constexpr int kTileQ = BM * D * 2;
+  static constexpr int kTileKV = BN * D * 2;
+  static constexpr int kTileP = BN * BM * 2;     // P^T / dS^T, bf16 [BN][BM]
+  static constexpr int kColBlocks = D / 64;
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kOffK + kTileKV;
+  static constexpr int kOffQ = kOffV + kTileKV;
+  static constexpr int kOffDO = kOffQ + NSQ * kTileQ;
+  static constexpr int kOffP = kOffDO + NSQ * kTileQ;
+  static constexpr int kOffStats = kOffP + kTileP;          // [NSQ][lse_log2[BM], delta[BM]]
+  static constexpr int kStatBytes = 2 * BM * 4;
+  static constexpr int kOffBar = kOffStats + NSQ * kStatBytes;
+  // barriers: KV, Qf[NSQ], Qe[NSQ], dOf[NSQ], dOe[NSQ], S, dP, P, dV, dS, dQf, dQfree, PdSfree
+  static constexpr int kNumBars = 1 + 4 * NSQ + 9;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
+};
+
+struct Params {
+  int Nq, Nkv, H;
+  int n_q_tiles;
+  int causal;
+  float scale_log2;
+  float scale;
+  int nq_pad;              // row pitch of the stats arrays (multiple of BM)
+  const float* lse2;       // [BH][nq_pad] LSE * log2(e), +inf past Nq
+  const float* delta;      // [BH][nq_pad], 0 past Nq
+  float* dq_acc;           // [BH][Nq][D]
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+};
+
+// Vector fp32 reduction into global memory (one 16-byte red).
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
 }
 
-extern "C" int pu_attn_bwd(const void*, const void*, const void*, const void*, const float*,
-                           const void*, void*, void*, void*, void*, size_t, int64_t, int64_t,
-                           int64_t, int64_t, int64_t, float, int, void*) {
-  return pu::set_error(PU_ERR_UNSUPPORTED, "backward not built yet");
+// Byte offset of the 16-byte chunk `chunk` (8 bf16) of row `row` in a
+// [rows][128] bf16 tile stored as two 64-column blocks with 128-byte swizzle
+// (the layout a 64x`rows` TMA box with CU_TENSOR_MAP_SWIZZLE_128B produces).
+__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk, int rows) {
+  const int cb = chunk >> 3;
+  const int c = chunk & 7;
+  return cb * rows * 128 + row * 128 + ((c ^ (row & 7)) << 4);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const Params p) {
+  using C = Cfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  if (smem_u32(smem) & 1023u) {  // the swizzled tiles need 1024-byte alignment
+    if (tid == 0) record_device_error(PU_ERR_UNSUPPORTED, kSiteBwdKV);
+    return;
+  }
+  uint8_t* sK = smem + C::kOffK;
+  uint8_t* sV = smem + C::kOffV;
+  uint8_t* sQ = smem + C::kOffQ;
+  uint8_t* sDO = smem + C::kOffDO;
+  uint8_t* sP = smem + C::kOffP;
+  float* s_stats = reinterpret_cast<float*>(smem + C::kOffStats);  // [NSQ][2][BM]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* bKV = bars;
+  uint64_t* bQf = bars + 1;
+  uint64_t* bQe = bQf + C::NSQ;
+  uint64_t* bDOf = bQe + C::NSQ;
+  uint64_t* bDOe = bDOf + C::NSQ;
+  uint64_t* bS = bDOe + C::NSQ;
+  uint64_t* bDP = bS + 1;
+  uint64_t* bP = bDP + 1;
+  uint64_t* bDV = bP + 1;
+  uint64_t* bDS = bDV + 1;
+  uint64_t* bDQf = bDS + 1;
+  uint64_t* bDQfree = bDQf + 1;
+  uint64_t* bPfree = bDQfree + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bPfree + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int bh = blockIdx.x;
+  const int kv_tile = blockIdx.y;
+  const int kv0 = kv_tile * BN;
+  const int first_q = p.causal ? min(kv0 / BM, p.n_q_tiles) : 0;
+  const int n_it = p.n_q_tiles - first_q;
+
+  if (tid == 128) {
+    mbar_init(bKV, 1);
+    for (int s = 0; s < C::NSQ; ++s) {
+      mbar_init(bQf + s, 1);
+      mbar_init(bQe + s, 1);
+      mbar_init(bDOf + s, 1);
+      mbar_init(bDOe + s, 1);
+    }
+    mbar_init(bS, 1);
+    mbar_init(bDP, 1);
+    mbar_init(bP, 128);
+    mbar_init(bDV, 1);
+    mbar_init(bDS, 128);
+    mbar_init(bDQf, 1);
+    mbar_init(bDQfree, 128);
+    mbar_init(bPfree, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && n_it > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmDO);
+      mbar_arrive_expect_tx(bKV, 2 * C::kTileKV);
+      for (int cb = 0; cb < C::kColBlocks; ++cb) {
+        tma_load_3d(sK + cb * BN * 128, &tmK, bKV, cb * 64, kv0, bh);
+        tma_load_3d(sV + cb * BN * 128, &tmV, bKV, cb * 64, kv0, bh);
+      }
+      for (int it = 0; it < n_it; ++it) {
+        const int st = it % C::NSQ;
+        const uint32_t u = it / C::NSQ;
+        const int q0 = (first_q + it) * BM;
+        if (u > 0 && !mbar_wait(bQe + st, (u - 1) & 1, abort_flag, kSiteBwdEmpty)) break;
+        mbar_arrive_expect_tx(bQf + st, C::kTileQ + C::kStatBytes);
+        for (int cb = 0; cb < C::kColBlocks; ++cb)
+          tma_load_3d(sQ + st * C::kTileQ + cb * BM * 128, &tmQ, bQf + st, cb * 64, q0, bh);
+        float* stat = s_stats + st * 2 * BM;
+        bulk_load(stat, p.lse2 + (size_t)bh * p.nq_pad + q0, BM * 4, bQf + st);
+        bulk_load(stat + BM, p.delta + (size_t)bh * p.nq_pad + q0, BM * 4, bQf + st);
+        if (u > 0 && !mbar_wait(bDOe + st, (u - 1) & 1, abort_flag, kSiteBwdEmpty)) break;
+        mbar_arrive_expect_tx(bDOf + st, C::kTileQ);
+        for (int cb = 0; cb < C::kColBlocks; ++cb)
+          tma_load_3d(sDO + st * C::kTileQ + cb * BM * 128, &tmDO, bDOf + st, cb * 64, q0, bh);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- tcgen05 issuer ----------------
+    if (lane == 0 && n_it > 0) {
+      constexpr uint32_t idSS = make_idesc_bf16(BN, BM, 0, 0);   // S^T, dP^T: K-major A and B
+      constexpr uint32_t idKMN = make_idesc_bf16(BN, D, 0, 1);   // dV, dK: A K-major, B MN-major
+      constexpr uint32_t idQ = make_idesc_bf16(BM, D, 1, 1);     // dQ: A (dS) MN-major, B (K) MN-major
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+      bool ok = mbar_wait(bKV, 0, abort_flag, kSiteBwdKV);
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % C::NSQ;
+        const uint32_t u = it / C::NSQ;
+        const uint32_t aQ = smem_u32(sQ + st * C::kTileQ);
+        const uint32_t aDO = smem_u32(sDO + st * C::kTileQ);
+        if (!mbar_wait(bQf + st, u & 1, abort_flag, kSiteBwdLoad)) break;
+        if (it > 0 && !mbar_wait(bDQfree, (it - 1) & 1, abort_flag, kSiteBwdDq)) break;
+        tc_fence_after();
+        // S^T = K Q^T
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          const uint32_t offq = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          mma_ss(tmem + kColS, make_sdesc_sw128(aK + off, 16, 1024), make_sdesc_sw128(aQ + offq, 16, 1024),
+                 idSS, kk > 0);
+        }
+        mma_commit(bS);
+        if (!mbar_wait(bDOf + st, u & 1, abort_flag, kSiteBwdLoad)) break;
+        tc_fence_after();
+        // dP^T = V dO^T
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          const uint32_t offq = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          mma_ss(tmem + kColDP, make_sdesc_sw128(aV + off, 16, 1024),
+                 make_sdesc_sw128(aDO + offq, 16, 1024), idSS, kk > 0);
+        }
+        mma_commit(bDP);
+        // dV += P^T dO   (A = P^T [kv][q] K-major; B = dO [q][d] MN-major)
+        if (!mbar_wait(bP, it & 1, abort_flag, kSiteBwdSoftmax)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk) {
+          const uint32_t offa = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          mma_ss(tmem + kColDV, make_sdesc_sw128(aP + offa, 16, 1024),
+                 make_sdesc_sw128(aDO + kk * 16 * 128, BM * 128, 1024), idKMN, (it > 0 || kk > 0));
+        }
+        mma_commit(bDV);
+        mma_commit(bDOe + st);
+        // dK += dS^T Q ; dQ = dS K
+        if (!mbar_wait(bDS, it & 1, abort_flag, kSiteBwdDs)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk) {
+          const uint32_t offa = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          mma_ss(tmem + kColDK, make_sdesc_sw128(aP + offa, 16, 1024),
+                 make_sdesc_sw128(aQ + kk * 16 * 128, BM * 128, 1024), idKMN, (it > 0 || kk > 0));
+        }
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          mma_ss(tmem + kColS, make_sdesc_sw128(aP + kk * 16 * 128, BN * 128, 1024),
+                 make_sdesc_sw128(aK + kk * 16 * 128, BN * 128, 1024), idQ, kk > 0);
+        }
+        mma_commit(bDQf);
+        mma_commit(bQe + st);
+        mma_commit(bPfree);
+      }
+    }
+  } else {
+    // ---------------- softmax / dS / dQ-drain warps 0-3 ----------------
+    const int r = tid;                                    // key row within the tile
+    const int kv_idx = kv0 + r;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    uint8_t* prow_base = sP;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = (first_q + it) * BM;
+      const int st = it % C::NSQ;
+      // the stage's row statistics (LSE*log2e, Delta) arrived with its Q tile
+      ok = mbar_wait(bQf + st, (it / C::NSQ) & 1, abort_flag, kSiteBwdLoad);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const float* lse_t = s_stats + st * 2 * BM;
+      const float* del_t = lse_t + BM;
+
+      ok = mbar_wait(bS, it & 1, abort_flag, kSiteBwdMma);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      // P^T row r (bf16 pairs)
+      uint32_t pk[BM / 2];
+      {
+        const bool need_mask = (p.causal && q0 < kv0 + BN - 1) || (q0 + BM > p.Nq) || (kv_idx >= p.Nkv);
+        uint32_t sr[32];
+#pragma unroll
+        for (int c = 0; c < BM / 32; ++c) {
+          tmem_ld32(tmem + lane_base + kColS + c * 32, sr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int col = c * 32 + i;
+            float p0 = ex2(fmaf(__uint_as_float(sr[i]), p.scale_log2, -lse_t[col]));
+            float p1 = ex2(fmaf(__uint_as_float(sr[i + 1]), p.scale_log2, -lse_t[col + 1]));
+            if (need_mask) {
+              const int qa = q0 + col;
+              if ((p.causal && qa < kv_idx) || qa >= p.Nq || kv_idx >= p.Nkv) p0 = 0.f;
+              if ((p.causal && qa + 1 < kv_idx) || qa + 1 >= p.Nq || kv_idx >= p.Nkv) p1 = 0.f;
+            }
+            pk[col / 2] = pack_bf16x2(p0, p1);
+          }
+        }
+      }
+      // the previous query tile's dK / dQ products must have read the tile
+      if (it > 0) {
+        ok = mbar_wait(bPfree, (it - 1) & 1, abort_flag, kSiteBwdDs);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int ch = 0; ch < BM / 8; ++ch) {
+        *reinterpret_cast<uint4*>(prow_base + sw128_offset(r, ch, BN)) =
+            make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bP);
+
+      // dS^T = P^T (dP^T - Delta)
+      ok = mbar_wait(bDP, it & 1, abort_flag, kSiteBwdMma);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      {
+        uint32_t dr[32];
+#pragma unroll
+        for (int c = 0; c < BM / 32; ++c) {
+          tmem_ld32(tmem + lane_base + kColDP + c * 32, dr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int col = c * 32 + i;
+            const uint32_t pp = pk[col / 2];
+            const float p0 = __uint_as_float(pp << 16);
+            const float p1 = __uint_as_float(pp & 0xFFFF0000u);
+            const float d0 = p0 * (__uint_as_float(dr[i]) - del_t[col]);
+            const float d1 = p1 * (__uint_as_float(dr[i + 1]) - del_t[col + 1]);
+            pk[col / 2] = pack_bf16x2(d0, d1);
+          }
+        }
+      }
+      // dV has consumed P^T: overwrite the tile with dS^T
+      ok = mbar_wait(bDV, it & 1, abort_flag, kSiteBwdMma);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+#pragma unroll
+      for (int ch = 0; ch < BM / 8; ++ch) {
+        *reinterpret_cast<uint4*>(prow_base + sw128_offset(r, ch, BN)) =
+            make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bDS);
+
+      // drain dQ_i (TMEM lane = query row) into the fp32 accumulator
+      ok = mbar_wait(bDQf, it & 1, abort_flag, kSiteBwdMma);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      {
+        const int qi = q0 + r;
+        float* dst = p.dq_acc + ((size_t)bh * p.Nq + qi) * D;
+        uint32_t qr[32];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tmem_ld32(tmem + lane_base + kColS + c * 32, qr);
+          tmem_wait_ld();
+          if (qi < p.Nq) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              red_add_v4(dst + c * 32 + i, __uint_as_float(qr[i]), __uint_as_float(qr[i + 1]),
+                         __uint_as_float(qr[i + 2]), __uint_as_float(qr[i + 3]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bDQfree);
+    }
+    // epilogue: dV, dK rows of this key tile (TMEM loads are warp-wide;
+    // only rows inside the sequence are stored)
+    if (ok) {
+      const bool store = kv_idx < p.Nkv;
+      __nv_bfloat16* dvrow = p.dv + ((size_t)bh * p.Nkv + kv_idx) * D;
+      __nv_bfloat16* dkrow = p.dk + ((size_t)bh * p.Nkv + kv_idx) * D;
+      if (n_it > 0) {
+        tc_fence_after();
+        uint32_t rr[32];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tmem_ld32(tmem + lane_base + kColDV + c * 32, rr);
+          tmem_wait_ld();
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1]));
+          uint4* dst = reinterpret_cast<uint4*>(dvrow + c * 32);
+          if (store) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tmem_ld32(tmem + lane_base + kColDK + c * 32, rr);
+          tmem_wait_ld();
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack_bf16x2(__uint_as_float(rr[2 * i]) * p.scale, __uint_as_float(rr[2 * i + 1]) * p.scale);
+          uint4* dst = reinterpret_cast<uint4*>(dkrow + c * 32);
+          if (store) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+      } else if (store) {
+        // no query attends to these keys: zero gradients
+        const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) {
+          reinterpret_cast<uint4*>(dvrow)[i] = z;
+          reinterpret_cast<uint4*>(dkrow)[i] = z;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Per row (b, h, i < nq_pad): delta = rowsum(dO * O), lse2 = LSE * log2(e)
+// (rows past Nq: +inf and 0), and dQ accumulator row := 0.  D/8 lanes per row.
+template <int D>
+__global__ void __launch_bounds__(256) prep_kernel(const __nv_bfloat16* __restrict__ o,
+                                                   const __nv_bfloat16* __restrict__ dout,
+                                                   const float* __restrict__ lse,
+                                                   float* __restrict__ lse2, float* __restrict__ delta,
+                                                   float* __restrict__ dq_acc, long long BH, int Nq,
+                                                   int nq_pad) {
+  constexpr int LPR = D / 8;
+  const long long gtid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long prow = gtid / LPR;                // padded row index
+  const int sub = (int)(gtid % LPR);
+  const long long bh = prow / nq_pad;
+  const int i = (int)(prow % nq_pad);
+  const bool valid = bh < BH && i < Nq;
+  const long long row = bh * Nq + i;                // dense row index
+  float acc = 0.f;
+  if (valid) {
+    const uint4 a = *reinterpret_cast<const uint4*>(o + row * D + sub * 8);
+    const uint4 b = *reinterpret_cast<const uint4*>(dout + row * D + sub * 8);
+    const uint32_t ua[4] = {a.x, a.y, a.z, a.w};
+    const uint32_t ub[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      acc = fmaf(__uint_as_float(ua[k] << 16), __uint_as_float(ub[k] << 16), acc);
+      acc = fmaf(__uint_as_float(ua[k] & 0xFFFF0000u), __uint_as_float(ub[k] & 0xFFFF0000u), acc);
+    }
+    float4* z = reinterpret_cast<float4*>(dq_acc + row * D + sub * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (bh < BH && sub == 0) {
+    delta[prow] = valid ? acc : 0.f;
+    lse2[prow] = valid ? lse[row] * kLog2e : INFINITY;
+  }
+}
+
+// dQ (bf16) = scale * accumulator; 8 elements per thread.
+__global__ void __launch_bounds__(256) post_kernel(const float* __restrict__ dq_acc,
+                                                   __nv_bfloat16* __restrict__ dq, float scale,
+                                                   long long n8) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const float4 a = reinterpret_cast<const float4*>(dq_acc)[2 * i];
+  const float4 b = reinterpret_cast<const float4*>(dq_acc)[2 * i + 1];
+  uint4 w;
+  w.x = pack_bf16x2(a.x * scale, a.y * scale);
+  w.y = pack_bf16x2(a.z * scale, a.w * scale);
+  w.z = pack_bf16x2(b.x * scale, b.y * scale);
+  w.w = pack_bf16x2(b.z * scale, b.w * scale);
+  reinterpret_cast<uint4*>(dq)[i] = w;
+}
+
+inline size_t round256(size_t x) { return (x + 255) / 256 * 256; }
+
+inline long long nq_padded(long long Nq) { return (Nq + BM - 1) / BM * BM; }
+
+// [dQ accumulator fp32 BH*Nq*D][lse2 fp32 BH*nq_pad][delta fp32 BH*nq_pad]
+inline size_t workspace_bytes(long long BH, long long Nq, long long D) {
+  return round256((size_t)BH * Nq * D * sizeof(float)) +
+         2 * round256((size_t)BH * nq_padded(Nq) * sizeof(float));
+}
+
+template <int D>
+int launch_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
+               const void* dout, void* dq, void* dk, void* dv, void* ws, long long B, long long H,
+               long long Nq, long long Nkv, float sm_scale, int causal, cudaStream_t st) {
+  using C = Cfg<D>;
+  const long long BH = B * H;
+  const long long nq_pad = nq_padded(Nq);
+  float* dq_acc = static_cast<float*>(ws);
+  float* lse2 = reinterpret_cast<float*>(static_cast<char*>(ws) + round256((size_t)BH * Nq * D * sizeof(float)));
+  float* delta = reinterpret_cast<float*>(reinterpret_cast<char*>(lse2) + round256((size_t)BH * nq_pad * sizeof(float)));
+  {
+    const long long threads = BH * nq_pad * (D / 8);
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    prep_kernel<D><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(o),
+                                           static_cast<const __nv_bfloat16*>(dout), lse, lse2, delta,
+                                           dq_acc, BH, (int)Nq, (int)nq_pad);
+    int rc = check_cuda(cudaGetLastError(), "backward prep launch");
+    if (rc) return rc;
+  }
+  CUtensorMap tq, tk, tv, tdo;
+  int rc = make_tmap_bf16_3d(&tq, q, D, Nq, BH, 64, BM, true);
+  if (!rc) rc = make_tmap_bf16_3d(&tk, k, D, Nkv, BH, 64, BN, true);
+  if (!rc) rc = make_tmap_bf16_3d(&tv, v, D, Nkv, BH, 64, BN, true);
+  if (!rc) rc = make_tmap_bf16_3d(&tdo, dout, D, Nq, BH, 64, BM, true);
+  if (rc) return rc;
+  static bool attr_done[64] = {false};
+  const int dev = current_device();
+  if (dev < 0) return PU_ERR_CUDA;
+  if (dev >= 64 || !attr_done[dev]) {
+    rc = check_cuda(cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes),
+                    "cudaFuncSetAttribute(bwd smem)");
+    if (rc) return rc;
+    if (dev < 64) attr_done[dev] = true;
+  }
+  Params prm{};
+  prm.Nq = (int)Nq;
+  prm.Nkv = (int)Nkv;
+  prm.H = (int)H;
+  prm.n_q_tiles = (int)((Nq + BM - 1) / BM);
+  prm.causal = causal ? 1 : 0;
+  prm.scale_log2 = sm_scale * kLog2e;
+  prm.scale = sm_scale;
+  prm.nq_pad = (int)nq_pad;
+  prm.lse2 = lse2;
+  prm.delta = delta;
+  prm.dq_acc = dq_acc;
+  prm.dk = static_cast<__nv_bfloat16*>(dk);
+  prm.dv = static_cast<__nv_bfloat16*>(dv);
+  const long long n_kv_tiles = (Nkv + BN - 1) / BN;
+  if (n_kv_tiles > 65535) return set_error(PU_ERR_UNSUPPORTED, "too many key tiles");
+  dim3 grid((unsigned)BH, (unsigned)n_kv_tiles);
+  attn_bwd_kernel<D><<<grid, kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, prm);
+  rc = check_cuda(cudaGetLastError(), "backward main launch");
+  if (rc) return rc;
+  const long long n8 = BH * Nq * D / 8;
+  post_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, st>>>(dq_acc, static_cast<__nv_bfloat16*>(dq),
+                                                            sm_scale, n8);
+  return check_cuda(cudaGetLastError(), "backward post launch");
+}
+
+}  // namespace bwd
+}  // namespace pu
+
+extern "C" size_t pu_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t Nq, int64_t D) {
+  if (B <= 0 || H <= 0 || Nq <= 0 || D <= 0) return 0;
+  return pu::bwd::workspace_bytes(B * H, Nq, D);
+}
+
+extern "C" int pu_attn_bwd(const void* q, const void* k, const void* v, const void* o,
+                           const float* lse, const void* dout, void* dq, void* dk, void* dv,
+                           void* workspace, size_t workspace_bytes, int64_t B, int64_t H,
+                           int64_t Nq, int64_t Nkv, int64_t D, float sm_scale, int causal,
+                           void* stream) {
+  using namespace pu::bwd;
+  int rc = pu::fwd::check_common(q, k, v, B, H, Nq, Nkv, D, sm_scale);
+  if (rc) return rc;
+  if (!o || !lse || !dout || !dq || !dk || !dv)
+    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null o/lse/dout/dq/dk/dv pointer");
+  if (!pu::aligned16(o) || !pu::aligned16(dout) || !pu::aligned16(dq) || !pu::aligned16(dk) ||
+      !pu::aligned16(dv))
+    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  const size_t need = pu::bwd::workspace_bytes(B * H, Nq, D);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return pu::set_error(PU_ERR_WORKSPACE, "backward workspace needs %zu bytes (256-aligned), got %zu",
+                         need, workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 128)
+    return launch_bwd<128>(q, k, v, o, lse, dout, dq, dk, dv, workspace, B, H, Nq, Nkv, sm_scale, causal, st);
+  return launch_bwd<64>(q, k, v, o, lse, dout, dq, dk, dv, workspace, B, H, Nq, Nkv, sm_scale, causal, st);
 }

@@ -138,11 +138,22 @@ __device__ __forceinline__ void tma_load_3d_hint(void* smem_dst, const void* des
       : "memory");
 }
 
+// Plain bulk copy global -> shared (16-byte aligned addresses, size a
+// multiple of 16), completing on an mbarrier.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // smem -> global tensor store (tile mode) and its completion wait.
 __device__ __forceinline__ void tma_store_3d(const void* desc, const void* smem_src, int c0, int c1,
                                              int c2) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(desc)),
       "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
@@ -152,8 +163,7 @@ __device__ __forceinline__ void tma_store_3d(const void* desc, const void* smem_
 __device__ __forceinline__ void tma_reduce_add_3d(const void* desc, const void* smem_src, int c0,
                                                   int c1, int c2) {
   asm volatile(
-      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], "
-      "[%1];" ::"l"(reinterpret_cast<uint64_t>(desc)),
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(desc)),
       "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
