@@ -1,0 +1,466 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention hot path (one JSON line on stdout).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl pu|reference]
+
+Headline workload (one "step", per GPU): causal flash-attention training
+forward + backward, B=4, H=16, N=4096, D=128, bf16, Q/K/V/dO ~ N(0,1)
+(the reference's training-attention configuration).  Under torchrun each
+rank owns its own 16 heads (heads are independent: no collective), so the
+per-GPU work is fixed and the job scales weakly; `value` is the aggregate
+TFLOP/s of all ranks, FLOPs counted as 4*B*H*N^2*D/2 forward (causal) and
+2.5x that backward (the reference's convention, benchmarks/scaling.py:44-54).
+
+The same line carries the split-KV decode measurement (B=1, H=32, a
+32768-token fp16 KV cache sharded by sequence over the N GPUs, NCCL
+all-gather of the (m, l, o) partials, fused LSE combine) as `decode`.
+
+`--impl reference` times the reference algorithm on the host CPU instead
+(the numpy restatement in oracle/, since the JAX reference cannot run
+here) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "pallas-unbound_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "attn fwd+bwd TFLOP/s (% BF16 peak); split-KV decode µs/step, HBM GB/s @1-8 GPU"
+B, H, N, D = 4, 16, 4096, 128
+DEC_B, DEC_H, DEC_N, DEC_D = 1, 32, 32768, 128
+FWD_FLOPS = 4 * B * H * N * N * D * 0.5          # causal
+STEP_FLOPS = FWD_FLOPS * 3.5                      # fwd + 2.5x bwd
+L2_BYTES = 126 * 1024 * 1024
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML, read-only)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples: list[tuple[float, int, int]] = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self._window = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: no clock record
+            self._nv = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM)
+                rs = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self._nv is not None:
+            self._t.start()
+        return self
+
+    def mark(self, t0, t1):
+        self._window = (t0, t1)
+
+    def stop(self) -> dict:
+        if self._nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        self._stop.set()
+        self._t.join(timeout=2)
+        win = [s for s in self.samples if self._window and self._window[0] <= s[0] <= self._window[1]]
+        used = win if win else self.samples
+        mhz = [s[1] for s in used]
+        bits = 0
+        for s in used:
+            bits |= s[2]
+        reasons = sorted({name for bit, name in self.REASONS.items() if bits & bit and name != "gpu_idle"})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(used), "in_window": bool(win)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_init():
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines (rank 0, N=1, bounded samples of the same workloads)
+# ---------------------------------------------------------------------------
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return max(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_attention_sample(heads: int = 2):
+    """Oracle fwd+bwd (numpy fp32) on `heads` heads of the B=4 H=16 N=4096 D=128 workload."""
+    import numpy as np
+    from oracle import attention as orc
+    rng = np.random.Generator(np.random.PCG64(1))
+    q = rng.standard_normal((1, heads, N, D), dtype=np.float32)
+    k = rng.standard_normal((1, heads, N, D), dtype=np.float32)
+    v = rng.standard_normal((1, heads, N, D), dtype=np.float32)
+    do = rng.standard_normal((1, heads, N, D), dtype=np.float32)
+    t0 = time.perf_counter()
+    o, lse = orc.mha_forward(q, k, v, causal=True, dtype=np.float32, row_chunk=N)
+    orc.mha_backward(q, k, v, o, lse, do, causal=True, dtype=np.float32, row_chunk=N)
+    dt = time.perf_counter() - t0
+    flops = STEP_FLOPS * heads / (B * H)
+    return flops / dt / 1e12, dt, f"{heads} of {B * H} (b,h) heads of the causal B4 H16 N4096 D128 fwd+bwd, numpy fp32"
+
+
+def cpu_decode_sample(heads: int = 8):
+    import numpy as np
+    from oracle import attention as orc
+    rng = np.random.Generator(np.random.PCG64(3))
+    q = rng.standard_normal((1, heads, 1, DEC_D)).astype(np.float16)
+    k = rng.standard_normal((1, heads, DEC_N, DEC_D)).astype(np.float16)
+    v = rng.standard_normal((1, heads, DEC_N, DEC_D)).astype(np.float16)
+    reps = 3
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        orc.decode_forward(q, k, v, dtype=np.float32)
+    dt = (time.perf_counter() - t0) / reps
+    us_full = dt * 1e6 * DEC_H / heads
+    return us_full, f"{heads} of {DEC_H} heads of the 32768-token fp16 decode, numpy fp32, scaled to 32 heads"
+
+
+# ---------------------------------------------------------------------------
+# GPU measurements
+# ---------------------------------------------------------------------------
+def bench_attention(steps: int, warmup: int, rank: int, world: int, clocks: ClockSampler):
+    import torch
+    from pallas_flash.ops import interface as pf
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1000 + rank)
+    shape = (B, H, N, D)
+    q, k, v, do = (torch.randn(shape, device="cuda", dtype=torch.float32, generator=g).to(torch.bfloat16)
+                   for _ in range(4))
+    o = torch.empty_like(q)
+    lse = torch.empty((B, H, N), device="cuda", dtype=torch.float32)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws = torch.empty(pf.bwd_workspace_bytes(B, H, N, D), device="cuda", dtype=torch.uint8)
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        pf.flash_attention_forward(q, k, v, causal=True, out=o, lse=lse)
+        if ev is not None:
+            ev[1].record(stream)
+        pf.flash_attention_backward(q, k, v, o, lse, do, causal=True, workspace=ws, dq=dq, dk=dk, dv=dv)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start.record(stream)
+    for i in range(steps):
+        step(evs[i])
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    barrier(world)
+    clocks.mark(t0, t1)
+    total_ms = start.elapsed_time(end)
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / steps
+    from pallas_flash import _lib
+    code, detail = _lib.device_status()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at site {detail}")
+    return total_ms, fwd_ms, bwd_ms
+
+
+def bench_attention_e2e(steps: int, warmup: int, rank: int, world: int):
+    """Through the public API with host (pinned) tensors: H2D of q, k, v, dO and
+    D2H of o, dq, dk, dv inside every timed step (torch.autograd drives the
+    backward through pallas_flash_attention)."""
+    import torch
+    from pallas_flash.ops.interface import pallas_flash_attention
+
+    g = torch.Generator()
+    g.manual_seed(2000 + rank)
+    shape = (B, H, N, D)
+    host = [torch.randn(shape, generator=g).to(torch.bfloat16).pin_memory() for _ in range(4)]
+    qh, kh, vh, doh = host
+    for t in (qh, kh, vh):
+        t.requires_grad_(True)
+
+    def step():
+        for t in (qh, kh, vh):
+            t.grad = None
+        o = pallas_flash_attention(qh, kh, vh, causal=True)    # H2D q,k,v ; D2H o
+        o.backward(doh)                                         # H2D dO ; D2H dq,dk,dv
+        return o
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / steps
+    dt = allreduce_max(dt, world)
+    nbytes = qh.numel() * 2
+    return dt, 4 * nbytes, 4 * nbytes
+
+
+def bench_decode(steps: int, warmup: int, rank: int, world: int):
+    import torch
+    from pallas_flash.kernels import decoding as dec
+
+    n_local = DEC_N // world
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3000 + rank)
+    q = torch.randn((DEC_B, DEC_H, 1, DEC_D), device="cuda", generator=g).to(torch.float16)
+    k = torch.randn((DEC_B, DEC_H, n_local, DEC_D), device="cuda", generator=g).to(torch.float16)
+    v = torch.randn((DEC_B, DEC_H, n_local, DEC_D), device="cuda", generator=g).to(torch.float16)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        group = dist.group.WORLD
+    stream = torch.cuda.current_stream()
+
+    def step():
+        return dec.pallas_flash_decoding(q, k, v, group=group)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    times = []
+    kern = []
+    for _ in range(steps):
+        flush.zero_()                               # evict the cache shard from L2
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    # kernel-only time of the local split-KV pass (pu_decode_partial / pu_decode)
+    part = torch.empty((DEC_B * DEC_H, DEC_D + 2), device="cuda", dtype=torch.float32)
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        if world == 1:
+            step()
+        else:
+            dec.decode_partial(q, k, v, kv_offset=rank * n_local, out=part)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        kern.append(e0.elapsed_time(e1))
+    barrier(world)
+    us = allreduce_max(statistics.median(times) * 1e3, world)
+    kus = allreduce_max(statistics.median(kern) * 1e3, world)
+    return us, kus, 2 * DEC_B * DEC_H * n_local * DEC_D * 2
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["pu", "reference"], default="pu")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    args = ap.parse_args()
+    warmup = max(3, args.warmup)
+    peaks = load_peaks()
+
+    if args.impl == "reference":
+        return run_reference(args, warmup)
+
+    import torch
+    rank, world, local = dist_init()
+    clocks = ClockSampler(local).start()
+    total_ms, fwd_ms, bwd_ms = bench_attention(args.steps, warmup, rank, world, clocks)
+    clk = clocks.stop()
+    ms_step = allreduce_max(total_ms / args.steps, world)
+    value = STEP_FLOPS * world / (ms_step * 1e-3) / 1e12
+    bwd_ms_max = allreduce_max(bwd_ms, world)
+    fwd_ms_max = allreduce_max(fwd_ms, world)
+    e2e_dt, h2d, d2h = bench_attention_e2e(max(1, args.e2e_steps), 1, rank, world)
+    dec_us, dec_kus, dec_bytes = bench_decode(max(5, min(args.steps, 50)), warmup, rank, world)
+
+    if rank == 0:
+        bwd_flops = FWD_FLOPS * 2.5
+        achieved = bwd_flops / (bwd_ms_max * 1e-3) / 1e12
+        roof = {"kernel": "attn_bwd (prep + tcgen05 main + dq post, one pu_attn_bwd call)",
+                "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                "peak_source": peaks["source"] + " bf16 burst",
+                "traffic": None}
+        fwd_ach = FWD_FLOPS / (fwd_ms_max * 1e-3) / 1e12
+        cpu = None
+        if world == 1:
+            cv, cdt, sample = cpu_attention_sample()
+            cpu = {"value": round(cv, 4), "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
+                   "sample": sample + f" ({cdt:.1f} s)"}
+        dec_total_bytes = dec_bytes * world
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic N(0,1) bf16 inputs generated on device (seeded)",
+            "config": {"workload": "causal flash-attention fwd+bwd, B=4 H=16 N=4096 D=128 bf16 per GPU "
+                                   "(heads partitioned across GPUs, no collective)",
+                       "global_batch": B, "seq_len": N, "heads_per_gpu": H, "global_heads": H * world,
+                       "head_dim": D, "parallelism": f"heads{world}",
+                       "l2": "inputs 268 MB per GPU > 126 MB L2 (no flush needed)"},
+            "roofline": roof,
+            "roofline_fwd": {"kernel": "attn_fwd", "achieved": round(fwd_ach, 1),
+                             "frac": round(fwd_ach / peaks["bf16_tflops"], 4), "unit": "TFLOP/s"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(STEP_FLOPS * world / e2e_dt / 1e12, 3), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_dt * 1e3, 3),
+                    "path": "pallas_flash_attention(host pinned q,k,v) + autograd backward"},
+            "gpu_launches": 4 * args.steps,
+            "clocks": clk,
+            "decode": {"workload": f"split-KV decode B=1 H=32 N=32768 D=128 fp16 cache, sequence-sharded over {world} GPU(s)"
+                                   + (", NCCL all-gather of (m,l,o) + fused combine" if world > 1 else ""),
+                       "us_per_step": round(dec_us, 2),
+                       "GB_s": round(dec_total_bytes / (dec_us * 1e-6) / 1e9, 1),
+                       "kernel_us": round(dec_kus, 2),
+                       "roofline": {"bound": "hbm", "achieved": round(dec_bytes / (dec_kus * 1e-6) / 1e9, 1),
+                                    "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                    "frac": round(dec_bytes / (dec_kus * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)},
+                       "l2": "256 MB buffer written before every step"},
+        }
+        if world == 1:
+            dus, dsample = cpu_decode_sample()
+            line["decode"]["cpu_baseline"] = {"value": round(dus, 1), "unit": "us/step",
+                                              "cores": cpu_threads(), "kind": "port", "sample": dsample}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args, warmup):
+    """The reference algorithm on host CPU cores (numpy port of its pure-JAX
+    path; JAX is not installed).  Rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    vals = []
+    sample = ""
+    for i in range(warmup + args.steps):
+        v, dt, sample = cpu_attention_sample(heads=1)
+        if i >= warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    # the CPU restatement is one host: its throughput does not grow with GPUs
+    step_ms = STEP_FLOPS * world / (value * 1e12) * 1e3
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": warmup, "ms_per_step": round(step_ms, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1) inputs (seeded numpy PCG64)",
+        "config": {"workload": "causal flash-attention fwd+bwd, B=4 H=16 N=4096 D=128 per GPU",
+                   "global_batch": B, "seq_len": N, "heads_per_gpu": H, "head_dim": D,
+                   "parallelism": f"heads{world}"},
+        "cpu_baseline": {"value": round(value, 4), "kind": "port", "cores": cpu_threads(),
+                         "sample": sample + " per step; JAX reference not installable here, so the "
+                                            "numpy restatement in oracle/ stands in"},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
