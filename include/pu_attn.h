@@ -166,6 +166,34 @@ PU_API int pu_decode(const void* q, int q_dtype,
               int64_t B, int64_t H, int64_t n, int64_t D,
               float sm_scale, void* stream);
 
+/*
+ * Allocation-free single-GPU decode step.  No counterpart in the reference:
+ * it exists for callers that have no way to hand over device scratch memory
+ * — for example a custom-call handler that receives only its operand and
+ * result buffers, or a serving runtime that plans all device memory at
+ * start-up and forbids allocation afterwards.  Same inputs, outputs and
+ * results as pu_decode, without the workspace arguments.
+ *   Scratch: a fixed 8 MiB array in the library's device memory, present on
+ *   every GPU that loads the library until the process exits.  A call needs
+ *   256 KiB + B*H*splits*(D+2)*4 bytes (splits = the split count pu_decode
+ *   chooses, about ceil(1184 / (B*H)) on a 148-SM B200); larger problems are
+ *   rejected with PU_ERR_WORKSPACE and a message, before anything is enqueued.
+ *   The entry point allocates nothing (no cudaMalloc/cudaFree, no library
+ *   allocator); it clears the scratch counters with cudaMemsetAsync on
+ *   `stream` before the kernel.
+ *   Set-up: the first call on each device looks up the array's device
+ *   address (cudaGetSymbolAddress) with that device current; make that first
+ *   call before any stream capture begins.
+ *   All calls on a device share the one array, so calls that overlap on the
+ *   GPU (different streams, no ordering between them) race and must not be
+ *   issued.
+ */
+PU_API int pu_decode_noalloc(const void* q, int q_dtype,
+                             const void* k_cache, const void* v_cache, int kv_dtype,
+                             const int32_t* kv_lens, void* o, float* lse,
+                             int64_t B, int64_t H, int64_t n, int64_t D,
+                             float sm_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

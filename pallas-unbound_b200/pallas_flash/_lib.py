@@ -50,6 +50,9 @@ SIGNATURES = {
     "pu_decode": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p,
                          _c_void_p, _c_void_p, _size_t, _i64, _i64, _i64, _i64, _float,
                          _c_void_p]),
+    "pu_decode_noalloc": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p,
+                                 _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _float,
+                                 _c_void_p]),
 }
 
 _lock = threading.Lock()
