@@ -132,8 +132,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bPfree + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int bh = blockIdx.x;
-  const int kv_tile = blockIdx.y;
+  // blockIdx.x walks the key tiles of one (b, h) — heaviest (causal: first)
+  // first — and blockIdx.y the (b, h): CTAs resident together share a few
+  // heads, so their Q/dO tiles and dQ accumulator rows stay in L2.
+  const int kv_tile = blockIdx.x;
+  const int bh = blockIdx.y;
   const int kv0 = kv_tile * BN;
   const int first_q = p.causal ? min(kv0 / BM, p.n_q_tiles) : 0;
   const int n_it = p.n_q_tiles - first_q;
@@ -550,8 +553,8 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
   prm.dk = static_cast<__nv_bfloat16*>(dk);
   prm.dv = static_cast<__nv_bfloat16*>(dv);
   const long long n_kv_tiles = (Nkv + BN - 1) / BN;
-  if (n_kv_tiles > 65535) return set_error(PU_ERR_UNSUPPORTED, "too many key tiles");
-  dim3 grid((unsigned)BH, (unsigned)n_kv_tiles);
+  if (BH > 65535) return set_error(PU_ERR_UNSUPPORTED, "B*H = %lld exceeds 65535", BH);
+  dim3 grid((unsigned)n_kv_tiles, (unsigned)BH);
   attn_bwd_kernel<D><<<grid, kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, prm);
   rc = check_cuda(cudaGetLastError(), "backward main launch");
   if (rc) return rc;

@@ -6,22 +6,28 @@
 // walks 128-row K/V blocks with an fp32 online softmax, P rounded to bf16
 // (low_level/intrinsics.py:33-37) before the P.V product.
 //
-// B200 design (one CTA per 128-row query tile of one (b, h)):
-//   warp 4      TMA producer: Q tile once, then K_j / V_j through an
-//               NS-deep ring of 128-row tiles (128-byte swizzle).
-//   warp 5      tcgen05 issuer (one thread) and TMEM owner:
-//                 S_j  = Q . K_j^T     (A, B from shared memory, K-major)
-//                 O   += P_j . V_j     (A = P from tensor memory, B = V
-//                                       MN-major from shared memory)
-//               S is double-buffered in TMEM so S_{j+1} runs on the tensor
-//               core while the softmax warps work on S_j.
-//   warps 0-3   softmax: thread r owns query row r (TMEM lane r), so row max
-//               and row sum need no shuffles.  Scores are scaled into log2
-//               units; the running max is only moved (and O, l rescaled)
-//               when it grows by more than kRescaleLog2, which keeps P <= 2^8.
-//               P goes to TMEM as bf16; the epilogue divides O by l, writes
-//               bf16 O and the fp32 natural-log LSE.
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O [256,256+D) P [384,448).
+// B200 design: one CTA owns two 128-row query tiles (256 rows) of one (b, h)
+// and streams every K/V block once for both.
+//   warp 8      TMA producer: Q tiles once, then K_j / V_j through NS-deep
+//               rings of 128-row tiles (128-byte swizzle).
+//   warp 9      tcgen05 issuer (one thread) and TMEM owner.  Per K/V block j:
+//                 O0 += P0_j V_j ; S0_{j+1} = Q0 K_{j+1}^T ;
+//                 O1 += P1_j V_j ; S1_{j+1} = Q1 K_{j+1}^T
+//               so the tensor core always has the other tile's work queued
+//               while a softmax warpgroup is busy.  P.V reads P from tensor
+//               memory (the `[d], [a], b_desc` form), V as an MN-major operand.
+//   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1: thread r owns
+//               query row r (TMEM lane r).  Scores are scaled into log2
+//               units; the running max only moves (O and l rescaled) when it
+//               grows by more than kRescaleLog2, so P <= 2^8.  P is written
+//               as bf16 over the first 64 columns of the tile's S columns.
+//               Partial maxima / sums in 8 independent accumulators keep the
+//               reductions from serialising on instruction latency.
+// TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
+// Ordering: the commit that signals S_t(j+1) also covers O_t += P_t(j) V_j
+// (issued earlier by the same thread), so a softmax warpgroup that has seen
+// S_t(j+1) may rescale O_t and overwrite P_t; S_t(j+1) itself is issued after
+// P_t(j) V_j and the tensor pipe executes one thread's MMAs in issue order.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -32,14 +38,16 @@
 namespace pu {
 namespace fwd {
 
-constexpr int BM = 128;             // query rows per CTA tile
+constexpr int BM = 128;             // query rows per tile (two tiles per CTA)
 constexpr int BN = 128;             // key/value rows per block
-constexpr int kThreads = 192;       // 4 softmax warps + producer + MMA
+constexpr int kThreads = 320;       // 2 softmax warpgroups + producer + MMA
 constexpr float kRescaleLog2 = 8.0f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256, kColP = 384;
+// TMEM column of tile t's S/P and O accumulators
+__host__ __device__ constexpr uint32_t col_s(int t) { return 128u * t; }
+__host__ __device__ constexpr uint32_t col_o(int t) { return 256u + 128u * t; }
 
 template <int D>
 struct Cfg {
@@ -47,19 +55,19 @@ struct Cfg {
   static constexpr int kTileQ = BM * D * 2;                // bytes
   static constexpr int kTileKV = BN * D * 2;
   static constexpr int kColBlocks = D / 64;                // 128-byte swizzle column blocks
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kTileQ;
+  static constexpr int kOffQ = 0;                          // two tiles
+  static constexpr int kOffK = kOffQ + 2 * kTileQ;
   static constexpr int kOffV = kOffK + NS * kTileKV;
   static constexpr int kOffBar = kOffV + NS * kTileKV;
-  // barriers: Q_full, K_full[NS], K_empty[NS], V_full[NS], V_empty[NS],
-  //           S_full[2], P_full, O_done; then tmem base + abort flag
-  static constexpr int kNumBars = 1 + 4 * NS + 2 + 2;
-  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + alignment slack
+  // barriers: Q_full[2], K_full[NS], K_empty[NS], V_full[NS], V_empty[NS],
+  //           S_full[2], P_full[2], O_final[2]; then tmem base + abort flag
+  static constexpr int kNumBars = 2 + 4 * NS + 6;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
 };
 
 struct Params {
   int Nq, Nkv, H;
-  int n_q_tiles;
+  int n_q_pairs;       // CTAs per (b, h): ceil(Nq / 256)
   int causal;
   float scale_log2;
   __nv_bfloat16* o;
@@ -71,50 +79,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const Params p) {
   using C = Cfg<D>;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  if (smem_u32(smem) & 1023u) {  // the swizzled tiles need 1024-byte alignment
+    if (tid == 0) record_device_error(PU_ERR_UNSUPPORTED, kSiteFwdQ);
+    return;
+  }
   uint8_t* sQ = smem + C::kOffQ;
   uint8_t* sK = smem + C::kOffK;
   uint8_t* sV = smem + C::kOffV;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-  uint64_t* bQ = bars;
-  uint64_t* bKf = bars + 1;
+  uint64_t* bQ = bars;              // [2]
+  uint64_t* bKf = bars + 2;
   uint64_t* bKe = bKf + C::NS;
   uint64_t* bVf = bKe + C::NS;
   uint64_t* bVe = bVf + C::NS;
-  uint64_t* bS = bVe + C::NS;   // [2]
-  uint64_t* bP = bS + 2;
-  uint64_t* bO = bP + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bO + 1);
+  uint64_t* bS = bVe + C::NS;       // [2]
+  uint64_t* bP = bS + 2;            // [2]
+  uint64_t* bOf = bP + 2;           // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bOf + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int bh = blockIdx.x;
-  // heaviest (causal: last) query tiles first
-  const int q_tile = p.n_q_tiles - 1 - blockIdx.y;
-  const int q0 = q_tile * BM;
-  const int n_kv_blocks_total = (p.Nkv + BN - 1) / BN;
-  int n_blocks = n_kv_blocks_total;
-  if (p.causal) n_blocks = min(n_blocks, (q0 + BM + BN - 1) / BN);
+  // blockIdx.x walks the 256-row query blocks of one (b, h) — heaviest
+  // (causal: last) first — and blockIdx.y the (b, h).
+  const int bh = blockIdx.y;
+  const int q0 = (p.n_q_pairs - 1 - (int)blockIdx.x) * (2 * BM);
+  const int n_kv_total = (p.Nkv + BN - 1) / BN;
+  int n_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    n_t[t] = n_kv_total;
+    if (p.causal) n_t[t] = max(1, min(n_kv_total, (q0 + t * BM + BM + BN - 1) / BN));
+  }
+  const int n_max = max(n_t[0], n_t[1]);
 
-  if (tid == 128) {
-    mbar_init(bQ, 1);
+  if (tid == 0) {
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bQ + t, 1);
+      mbar_init(bS + t, 1);
+      mbar_init(bP + t, 128);
+      mbar_init(bOf + t, 1);
+    }
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(bKf + s, 1);
       mbar_init(bKe + s, 1);
       mbar_init(bVf + s, 1);
       mbar_init(bVe + s, 1);
     }
-    mbar_init(bS, 1);
-    mbar_init(bS + 1, 1);
-    mbar_init(bP, 128);
-    mbar_init(bO, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -123,16 +140,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(bQ, C::kTileQ);
-      for (int cb = 0; cb < C::kColBlocks; ++cb)
-        tma_load_3d(sQ + cb * BM * 128, &tmQ, bQ, cb * 64, q0, bh);
-      for (int j = 0; j < n_blocks; ++j) {
+      for (int t = 0; t < 2; ++t) {
+        mbar_arrive_expect_tx(bQ + t, C::kTileQ);
+        for (int cb = 0; cb < C::kColBlocks; ++cb)
+          tma_load_3d(sQ + t * C::kTileQ + cb * BM * 128, &tmQ, bQ + t, cb * 64, q0 + t * BM, bh);
+      }
+      for (int j = 0; j < n_max; ++j) {
         const int st = j % C::NS;
         const uint32_t u = j / C::NS;
         if (u > 0 && !mbar_wait(bKe + st, (u - 1) & 1, abort_flag, kSiteFwdKEmpty)) break;
@@ -145,86 +164,111 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(sV + st * C::kTileKV + cb * BN * 128, &tmV, bVf + st, cb * 64, j * BN, bh);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- tcgen05 issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idS = make_idesc_bf16(BM, BN, 0, 0);
       constexpr uint32_t idO = make_idesc_bf16(BM, D, 0, 1);
-      const uint32_t aQ = smem_u32(sQ);
-      bool ok = mbar_wait(bQ, 0, abort_flag, kSiteFwdQ);
-      auto issue_S = [&](int j) -> bool {
-        const int st = j % C::NS;
-        if (!mbar_wait(bKf + st, (j / C::NS) & 1, abort_flag, kSiteFwdKFull)) return false;
-        tc_fence_after();
-        const uint32_t aK = smem_u32(sK + st * C::kTileKV);
-        const uint32_t dS = tmem + ((j & 1) ? kColS1 : kColS0);
+      auto issue_S = [&](int t, int j) {
+        const uint32_t aQ = smem_u32(sQ + t * C::kTileQ);
+        const uint32_t aK = smem_u32(sK + (j % C::NS) * C::kTileKV);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint32_t offk = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          mma_ss(dS, make_sdesc_sw128(aQ + off, 16, 1024), make_sdesc_sw128(aK + offk, 16, 1024), idS,
-                 kk > 0);
+          mma_ss(tmem + col_s(t), make_sdesc_sw128(aQ + off, 16, 1024),
+                 make_sdesc_sw128(aK + offk, 16, 1024), idS, kk > 0);
         }
-        mma_commit(bS + (j & 1));
-        mma_commit(bKe + st);
-        return true;
+        mma_commit(bS + t);
       };
-      if (ok) ok = issue_S(0);
-      for (int j = 0; ok && j < n_blocks; ++j) {
-        if (j + 1 < n_blocks && !issue_S(j + 1)) break;
-        if (!mbar_wait(bP, j & 1, abort_flag, kSiteFwdPFull)) break;
-        const int st = j % C::NS;
-        if (!mbar_wait(bVf + st, (j / C::NS) & 1, abort_flag, kSiteFwdVFull)) break;
-        tc_fence_after();
-        const uint32_t aV = smem_u32(sV + st * C::kTileKV);
+      auto issue_PV = [&](int t, int j) {
+        const uint32_t aV = smem_u32(sV + (j % C::NS) * C::kTileKV);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          mma_ts(tmem + kColO, tmem + kColP + kk * 8, make_sdesc_sw128(aV + kk * 16 * 128, BN * 128, 1024),
-                 idO, (j > 0 || kk > 0));
+          mma_ts(tmem + col_o(t), tmem + col_s(t) + kk * 8,
+                 make_sdesc_sw128(aV + kk * 16 * 128, BN * 128, 1024), idO, (j > 0 || kk > 0));
         }
-        mma_commit(bO);
+      };
+      bool ok = mbar_wait(bKf, 0, abort_flag, kSiteFwdKFull);
+      for (int t = 0; ok && t < 2; ++t) {
+        ok = mbar_wait(bQ + t, 0, abort_flag, kSiteFwdQ);
+        if (!ok) break;
+        tc_fence_after();
+        issue_S(t, 0);
+      }
+      if (ok) mma_commit(bKe);
+      for (int j = 0; ok && j < n_max; ++j) {
+        const int st = j % C::NS;
+        const int nst = (j + 1) % C::NS;
+        if (!mbar_wait(bVf + st, (j / C::NS) & 1, abort_flag, kSiteFwdVFull)) break;
+        const bool next_k = (j + 1 < n_max);
+        bool k_ready = false;
+        for (int t = 0; t < 2; ++t) {
+          if (j >= n_t[t]) continue;
+          if (!mbar_wait(bP + t, j & 1, abort_flag, kSiteFwdPFull)) { ok = false; break; }
+          tc_fence_after();
+          issue_PV(t, j);
+          if (j + 1 < n_t[t]) {
+            if (!k_ready) {
+              if (!mbar_wait(bKf + nst, ((j + 1) / C::NS) & 1, abort_flag, kSiteFwdKFull)) { ok = false; break; }
+              tc_fence_after();
+              k_ready = true;
+            }
+            issue_S(t, j + 1);
+          } else {
+            mma_commit(bOf + t);
+          }
+        }
+        if (!ok) break;
         mma_commit(bVe + st);
+        if (next_k) mma_commit(bKe + nst);
       }
     }
   } else {
-    // ---------------- softmax warps 0-3 ----------------
-    const int row = tid;                       // TMEM lane == query row in tile
-    const int q_idx = q0 + row;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    // ---------------- softmax warpgroups (warps 0-3: tile 0, 4-7: tile 1) ----------------
+    const int t = warp >> 2;
+    const int row = tid & 127;                 // TMEM lane == query row in tile
+    const int q_tile0 = q0 + t * BM;
+    const int q_idx = q_tile0 + row;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + col_s(t);
+    const uint32_t tO = tmem + lane_base + col_o(t);
+    const int n_blocks = n_t[t];
     float m_ref = -INFINITY;                   // log2 domain
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_blocks; ++j) {
-      ok = mbar_wait(bS + (j & 1), (j >> 1) & 1, abort_flag, kSiteFwdSFull);
+      ok = mbar_wait(bS + t, j & 1, abort_flag, kSiteFwdSFull);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t tS = tmem + lane_base + ((j & 1) ? kColS1 : kColS0);
-      float s[BN];
+      uint32_t s[BN];
       {
-        uint32_t r[32];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(tS + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-        }
+        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(s);
+        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(s + 32);
+        uint32_t (&s2)[32] = *reinterpret_cast<uint32_t(*)[32]>(s + 64);
+        uint32_t (&s3)[32] = *reinterpret_cast<uint32_t(*)[32]>(s + 96);
+        tmem_ld32(tS, s0);
+        tmem_ld32(tS + 32, s1);
+        tmem_ld32(tS + 64, s2);
+        tmem_ld32(tS + 96, s3);
+        tmem_wait_ld();
+        reg_fence(s);
       }
       const int kv0 = j * BN;
-      if (p.causal && kv0 + BN - 1 > q0) {
+      if ((p.causal && kv0 + BN - 1 > q_tile0) || kv0 + BN > p.Nkv) {
+        const int lim = p.causal ? min(q_idx + 1, p.Nkv) : p.Nkv;   // keys < lim are visible
 #pragma unroll
         for (int c = 0; c < BN; ++c)
-          if (kv0 + c > q_idx) s[c] = -INFINITY;
+          if (kv0 + c >= lim) s[c] = __float_as_uint(-INFINITY);
       }
-      if (kv0 + BN > p.Nkv) {
+      float mx8[8];
 #pragma unroll
-        for (int c = 0; c < BN; ++c)
-          if (kv0 + c >= p.Nkv) s[c] = -INFINITY;
-      }
-      float mx = s[0];
+      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(s[i]);
 #pragma unroll
-      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(s[c]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_blk = mx * p.scale_log2;
       float alpha = 1.f;
       if (j == 0) {
@@ -233,62 +277,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         alpha = ex2(m_ref - m_blk);
         m_ref = m_blk;
       }
-      const float neg_m = -m_ref;
-      float rs = 0.f;
-      uint32_t pk[BN / 2];
-#pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        const float p0 = ex2(fmaf(s[c], p.scale_log2, neg_m));
-        const float p1 = ex2(fmaf(s[c + 1], p.scale_log2, neg_m));
-        rs += p0 + p1;
-        pk[c / 2] = pack_bf16x2(p0, p1);
-      }
-      // P_{j-1}.V_{j-1} must be done before O is rescaled or P overwritten
-      if (j > 0) {
-        ok = mbar_wait(bO, (j - 1) & 1, abort_flag, kSiteFwdODone);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      // O_t is quiescent: the commit behind S_t(j) covered O_t += P_t(j-1) V_{j-1}
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
+          tmem_ld32(tO + c * 32, r);
+          tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            const uint32_t tO = tmem + lane_base + kColO + c * 32;
-            tmem_ld32(tO, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tO, r);
-          }
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tO + c * 32, r);
         }
       }
+      const float neg_m = -m_ref;
+      float rs8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = h * 64 + 2 * i;
+          const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, neg_m));
+          const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, neg_m));
+          rs8[(2 * i) & 7] += p0;
+          rs8[(2 * i + 1) & 7] += p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st32(tS + h * 32, pk);
+      }
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
-      {
-        uint32_t r[32];
-#pragma unroll
-        for (int c = 0; c < BN / 64; ++c) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = pk[c * 32 + i];
-          tmem_st32(tmem + lane_base + kColP + c * 32, r);
-        }
-      }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bP);
+      mbar_arrive(bP + t);
     }
-    if (ok && n_blocks > 0) {
-      ok = mbar_wait(bO, (n_blocks - 1) & 1, abort_flag, kSiteFwdODone);
+    if (ok) {
+      ok = mbar_wait(bOf + t, 0, abort_flag, kSiteFwdODone);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
       tc_fence_after();
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.o + ((size_t)bh * p.Nq + q_idx) * D;
-      uint32_t r[32];
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
-        tmem_ld32(tmem + lane_base + kColO + c * 32, r);
+        uint32_t r[32];
+        tmem_ld32(tO + c * 32, r);
         tmem_wait_ld();
+        reg_fence(r);
         if (q_idx < p.Nq) {
           uint32_t w[16];
 #pragma unroll
@@ -307,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -321,7 +360,7 @@ inline int check_common(const void* q, const void* k, const void* v, long long B
   if (D != 128 && D != 64)
     return set_error(PU_ERR_UNSUPPORTED, "head size %lld (supported: 64, 128; pad others)", D);
   if (!(sm_scale > 0.f)) return set_error(PU_ERR_INVALID_ARGUMENT, "sm_scale must be > 0");
-  if (B * H > 0x7fffffffll) return set_error(PU_ERR_UNSUPPORTED, "B*H too large");
+  if (B * H > 65535) return set_error(PU_ERR_UNSUPPORTED, "B*H = %lld exceeds 65535", B * H);
   if (Nq > (1ll << 24) || Nkv > (1ll << 24))
     return set_error(PU_ERR_UNSUPPORTED, "sequence length above 2^24");
   return PU_OK;
@@ -350,13 +389,12 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   prm.Nq = (int)Nq;
   prm.Nkv = (int)Nkv;
   prm.H = (int)H;
-  prm.n_q_tiles = (int)((Nq + BM - 1) / BM);
+  prm.n_q_pairs = (int)((Nq + 2 * BM - 1) / (2 * BM));
   prm.causal = causal ? 1 : 0;
   prm.scale_log2 = sm_scale * kLog2e;
   prm.o = static_cast<__nv_bfloat16*>(o);
   prm.lse = lse;
-  if (prm.n_q_tiles > 65535) return set_error(PU_ERR_UNSUPPORTED, "too many query tiles");
-  dim3 grid((unsigned)(B * H), (unsigned)prm.n_q_tiles);
+  dim3 grid((unsigned)prm.n_q_pairs, (unsigned)(B * H));
   attn_fwd_kernel<D><<<grid, kThreads, C::kSmemBytes, st>>>(tq, tk, tv, prm);
   return check_cuda(cudaGetLastError(), "attention forward launch");
 }
