@@ -9,25 +9,28 @@
 //   dQ = scale * dS K,           dK = scale * dS^T Q.
 //
 // Three kernels:
-//   prep   : Delta[b,h,i] (fp32) and zeroing of the fp32 dQ accumulator.
+//   prep   : Delta (fp32), LSE in log2 units, zeroed fp32 dQ accumulator.
 //   main   : one CTA per 128-row K/V tile of one (b, h); K and V stay in
-//            shared memory while 128-row Q / dO tiles stream through a
-//            2-deep TMA ring.  Per query tile (transposed formulation, TMEM
-//            lanes = key rows):
+//            shared memory while 128-row Q / dO tiles (with their LSE/Delta)
+//            stream through 2-deep TMA rings.  Per query tile, with TMEM
+//            lanes = key rows:
 //              S^T  = K Q^T      -> TMEM [0,128)
 //              dP^T = V dO^T     -> TMEM [128,256)
-//              softmax warps: P^T = exp2(S^T*scale*log2e - LSE*log2e) (bf16,
-//                into shared memory), then dS^T = P^T (dP^T - Delta)
+//              P^T  = exp2(S^T*scale*log2e - LSE*log2e)  (bf16, shared memory)
 //              dV  += P^T dO     -> TMEM [256,256+D)
+//              dS^T = P^T (dP^T - Delta)                  (bf16, over P^T)
 //              dK  += dS^T Q     -> TMEM [384,384+D)
-//              dQ_i = dS K       -> TMEM [0,D) (reuses S^T's columns), drained
-//                                   by the softmax warps into the fp32 dQ
-//                                   accumulator with vector reductions.
-//            P^T and dS^T share one shared-memory tile (dS^T is written once
-//            the dV product has consumed P^T).
+//              dQ_i = dS K       -> TMEM [128,128+D) (dP^T's columns)
+//            S^T of the next query tile is issued right after dQ_i, so the
+//            tensor core works on it while dQ_i is drained.
 //   post   : dQ = bf16(scale * dQ accumulator).
-// Warp roles of the main kernel as in the forward: warps 0-3 softmax/drain,
-// warp 4 TMA producer, warp 5 tcgen05 issuer + TMEM owner.
+// Warp roles of the main kernel:
+//   warps 0-3  P^T and dS^T (thread r = key row r), then the dK/dV epilogue.
+//   warps 4-7  dQ drain: each warp takes 32 query rows of dQ_i from TMEM,
+//              stages 32x32 fp32 chunks (128-byte swizzle) in the P^T/dS^T
+//              tile once the MMAs have read it, and adds them into the fp32
+//              accumulator with TMA bulk tensor reductions.
+//   warp 8     TMA producer.   warp 9  tcgen05 issuer + TMEM owner.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -40,7 +43,7 @@ namespace bwd {
 
 constexpr int BM = 128;   // query rows per streamed tile
 constexpr int BN = 128;   // key/value rows per CTA
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 384;
@@ -50,7 +53,7 @@ struct Cfg {
   static constexpr int NSQ = 2;                  // Q / dO ring depth
   static constexpr int kTileQ = BM * D * 2;
   static constexpr int kTileKV = BN * D * 2;
-  static constexpr int kTileP = BN * BM * 2;     // P^T / dS^T, bf16 [BN][BM]
+  static constexpr int kTileP = BN * BM * 2;     // P^T / dS^T, bf16 [BN][BM]; dQ staging
   static constexpr int kColBlocks = D / 64;
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kTileKV;
@@ -60,9 +63,11 @@ struct Cfg {
   static constexpr int kOffStats = kOffP + kTileP;          // [NSQ][lse_log2[BM], delta[BM]]
   static constexpr int kStatBytes = 2 * BM * 4;
   static constexpr int kOffBar = kOffStats + NSQ * kStatBytes;
-  // barriers: KV, Qf[NSQ], Qe[NSQ], dOf[NSQ], dOe[NSQ], S, dP, P, dV, dS, dQf, dQfree, PdSfree
-  static constexpr int kNumBars = 1 + 4 * NSQ + 9;
+  // barriers: KV, Qf[NSQ], Qe[NSQ], dOf[NSQ], dOe[NSQ], S, dP, P, dV, dS, dQf,
+  //           dQfree, PdSfree, final
+  static constexpr int kNumBars = 1 + 4 * NSQ + 10;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct Params {
@@ -74,17 +79,9 @@ struct Params {
   int nq_pad;              // row pitch of the stats arrays (multiple of BM)
   const float* lse2;       // [BH][nq_pad] LSE * log2(e), +inf past Nq
   const float* delta;      // [BH][nq_pad], 0 past Nq
-  float* dq_acc;           // [BH][Nq][D]
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
 };
-
-// Vector fp32 reduction into global memory (one 16-byte red).
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
-}
 
 // Byte offset of the 16-byte chunk `chunk` (8 bf16) of row `row` in a
 // [rows][128] bf16 tile stored as two 64-column blocks with 128-byte swizzle
@@ -99,7 +96,7 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const Params p) {
+                    const __grid_constant__ CUtensorMap tmDQ, const Params p) {
   using C = Cfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
@@ -129,7 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bDQf = bDS + 1;
   uint64_t* bDQfree = bDQf + 1;
   uint64_t* bPfree = bDQfree + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bPfree + 1);
+  uint64_t* bFinal = bPfree + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bFinal + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   // blockIdx.x walks the key tiles of one (b, h) — heaviest (causal: first)
@@ -141,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int first_q = p.causal ? min(kv0 / BM, p.n_q_tiles) : 0;
   const int n_it = p.n_q_tiles - first_q;
 
-  if (tid == 128) {
+  if (tid == 0) {
     mbar_init(bKV, 1);
     for (int s = 0; s < C::NSQ; ++s) {
       mbar_init(bQf + s, 1);
@@ -156,11 +154,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bDS, 128);
     mbar_init(bDQf, 1);
     mbar_init(bDQfree, 128);
-    mbar_init(bPfree, 1);
+    mbar_init(bPfree, 4);
+    mbar_init(bFinal, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -169,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0 && n_it > 0) {
       tma_prefetch_desc(&tmQ);
@@ -198,23 +197,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(sDO + st * C::kTileQ + cb * BM * 128, &tmDO, bDOf + st, cb * 64, q0, bh);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- tcgen05 issuer ----------------
     if (lane == 0 && n_it > 0) {
       constexpr uint32_t idSS = make_idesc_bf16(BN, BM, 0, 0);   // S^T, dP^T: K-major A and B
       constexpr uint32_t idKMN = make_idesc_bf16(BN, D, 0, 1);   // dV, dK: A K-major, B MN-major
       constexpr uint32_t idQ = make_idesc_bf16(BM, D, 1, 1);     // dQ: A (dS) MN-major, B (K) MN-major
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-      bool ok = mbar_wait(bKV, 0, abort_flag, kSiteBwdKV);
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int st = it % C::NSQ;
-        const uint32_t u = it / C::NSQ;
-        const uint32_t aQ = smem_u32(sQ + st * C::kTileQ);
-        const uint32_t aDO = smem_u32(sDO + st * C::kTileQ);
-        if (!mbar_wait(bQf + st, u & 1, abort_flag, kSiteBwdLoad)) break;
-        if (it > 0 && !mbar_wait(bDQfree, (it - 1) & 1, abort_flag, kSiteBwdDq)) break;
-        tc_fence_after();
-        // S^T = K Q^T
+      auto issue_S = [&](int it) {
+        const uint32_t aQ = smem_u32(sQ + (it % C::NSQ) * C::kTileQ);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
@@ -223,9 +214,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                  idSS, kk > 0);
         }
         mma_commit(bS);
-        if (!mbar_wait(bDOf + st, u & 1, abort_flag, kSiteBwdLoad)) break;
+      };
+      bool ok = mbar_wait(bKV, 0, abort_flag, kSiteBwdKV) && mbar_wait(bQf, 0, abort_flag, kSiteBwdLoad);
+      if (ok) {
         tc_fence_after();
-        // dP^T = V dO^T
+        issue_S(0);
+      }
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % C::NSQ;
+        const uint32_t u = it / C::NSQ;
+        const uint32_t aQ = smem_u32(sQ + st * C::kTileQ);
+        const uint32_t aDO = smem_u32(sDO + st * C::kTileQ);
+        // dP^T = V dO^T into dP's columns once dQ_{it-1} has been drained from them
+        if (!mbar_wait(bDOf + st, u & 1, abort_flag, kSiteBwdLoad)) break;
+        if (it > 0 && !mbar_wait(bDQfree, (it - 1) & 1, abort_flag, kSiteBwdDq)) break;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bDV);
         mma_commit(bDOe + st);
-        // dK += dS^T Q ; dQ = dS K
+        // dK += dS^T Q ; dQ_it = dS K (into dP's columns)
         if (!mbar_wait(bDS, it & 1, abort_flag, kSiteBwdDs)) break;
         tc_fence_after();
 #pragma unroll
@@ -256,20 +259,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          mma_ss(tmem + kColS, make_sdesc_sw128(aP + kk * 16 * 128, BN * 128, 1024),
+          mma_ss(tmem + kColDP, make_sdesc_sw128(aP + kk * 16 * 128, BN * 128, 1024),
                  make_sdesc_sw128(aK + kk * 16 * 128, BN * 128, 1024), idQ, kk > 0);
         }
         mma_commit(bDQf);
         mma_commit(bQe + st);
-        mma_commit(bPfree);
+        // next query tile's S^T (S columns were read before P^T was published)
+        if (it + 1 < n_it) {
+          const int nst = (it + 1) % C::NSQ;
+          if (!mbar_wait(bQf + nst, ((it + 1) / C::NSQ) & 1, abort_flag, kSiteBwdLoad)) break;
+          tc_fence_after();
+          issue_S(it + 1);
+        } else {
+          mma_commit(bFinal);
+        }
       }
     }
-  } else {
-    // ---------------- softmax / dS / dQ-drain warps 0-3 ----------------
+  } else if (warp < 4) {
+    // ---------------- P^T / dS^T warps 0-3, then the dK/dV epilogue ----------------
     const int r = tid;                                    // key row within the tile
     const int kv_idx = kv0 + r;
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    uint8_t* prow_base = sP;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
       const int q0 = (first_q + it) * BM;
@@ -285,30 +295,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      // P^T row r (bf16 pairs)
       uint32_t pk[BM / 2];
       {
         const bool need_mask = (p.causal && q0 < kv0 + BN - 1) || (q0 + BM > p.Nq) || (kv_idx >= p.Nkv);
-        uint32_t sr[32];
+        const int lo = p.causal ? kv_idx : 0;     // key kv_idx is visible to queries >= lo
+        const bool kv_ok = kv_idx < p.Nkv;
 #pragma unroll
-        for (int c = 0; c < BM / 32; ++c) {
-          tmem_ld32(tmem + lane_base + kColS + c * 32, sr);
+        for (int h = 0; h < 2; ++h) {           // two halves of 64 columns: bounded registers
+          uint32_t sr[64];
+          tmem_ld32(tmem + lane_base + kColS + h * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
+          tmem_ld32(tmem + lane_base + kColS + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
           tmem_wait_ld();
+          reg_fence(sr);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int col = c * 32 + i;
-            float p0 = ex2(fmaf(__uint_as_float(sr[i]), p.scale_log2, -lse_t[col]));
-            float p1 = ex2(fmaf(__uint_as_float(sr[i + 1]), p.scale_log2, -lse_t[col + 1]));
+          for (int c4 = 0; c4 < 64; c4 += 4) {
+            const int col = h * 64 + c4;
+            const float4 lv = *reinterpret_cast<const float4*>(lse_t + col);
+            float p0 = ex2(fmaf(__uint_as_float(sr[c4]), p.scale_log2, -lv.x));
+            float p1 = ex2(fmaf(__uint_as_float(sr[c4 + 1]), p.scale_log2, -lv.y));
+            float p2 = ex2(fmaf(__uint_as_float(sr[c4 + 2]), p.scale_log2, -lv.z));
+            float p3 = ex2(fmaf(__uint_as_float(sr[c4 + 3]), p.scale_log2, -lv.w));
             if (need_mask) {
               const int qa = q0 + col;
-              if ((p.causal && qa < kv_idx) || qa >= p.Nq || kv_idx >= p.Nkv) p0 = 0.f;
-              if ((p.causal && qa + 1 < kv_idx) || qa + 1 >= p.Nq || kv_idx >= p.Nkv) p1 = 0.f;
+              if (!(kv_ok && qa >= lo && qa < p.Nq)) p0 = 0.f;
+              if (!(kv_ok && qa + 1 >= lo && qa + 1 < p.Nq)) p1 = 0.f;
+              if (!(kv_ok && qa + 2 >= lo && qa + 2 < p.Nq)) p2 = 0.f;
+              if (!(kv_ok && qa + 3 >= lo && qa + 3 < p.Nq)) p3 = 0.f;
             }
             pk[col / 2] = pack_bf16x2(p0, p1);
+            pk[col / 2 + 1] = pack_bf16x2(p2, p3);
           }
         }
       }
-      // the previous query tile's dK / dQ products must have read the tile
+      // the drain of dQ_{it-1} must have finished reading its staging from the tile
       if (it > 0) {
         ok = mbar_wait(bPfree, (it - 1) & 1, abort_flag, kSiteBwdDs);
         ok = __all_sync(0xffffffffu, ok);
@@ -316,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int ch = 0; ch < BM / 8; ++ch) {
-        *reinterpret_cast<uint4*>(prow_base + sw128_offset(r, ch, BN)) =
+        *reinterpret_cast<uint4*>(sP + sw128_offset(r, ch, BN)) =
             make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
       }
       fence_proxy_async_smem();
@@ -327,94 +346,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      {
-        uint32_t dr[32];
 #pragma unroll
-        for (int c = 0; c < BM / 32; ++c) {
-          tmem_ld32(tmem + lane_base + kColDP + c * 32, dr);
-          tmem_wait_ld();
+      for (int h = 0; h < 2; ++h) {
+        uint32_t dr[64];
+        tmem_ld32(tmem + lane_base + kColDP + h * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
+        tmem_ld32(tmem + lane_base + kColDP + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+        tmem_wait_ld();
+        reg_fence(dr);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int col = c * 32 + i;
-            const uint32_t pp = pk[col / 2];
-            const float p0 = __uint_as_float(pp << 16);
-            const float p1 = __uint_as_float(pp & 0xFFFF0000u);
-            const float d0 = p0 * (__uint_as_float(dr[i]) - del_t[col]);
-            const float d1 = p1 * (__uint_as_float(dr[i + 1]) - del_t[col + 1]);
-            pk[col / 2] = pack_bf16x2(d0, d1);
-          }
+        for (int c4 = 0; c4 < 64; c4 += 4) {
+          const int col = h * 64 + c4;
+          const float4 dl = *reinterpret_cast<const float4*>(del_t + col);
+          const uint32_t pa = pk[col / 2], pb = pk[col / 2 + 1];
+          const float e0 = __uint_as_float(pa << 16) * (__uint_as_float(dr[c4]) - dl.x);
+          const float e1 = __uint_as_float(pa & 0xFFFF0000u) * (__uint_as_float(dr[c4 + 1]) - dl.y);
+          const float e2 = __uint_as_float(pb << 16) * (__uint_as_float(dr[c4 + 2]) - dl.z);
+          const float e3 = __uint_as_float(pb & 0xFFFF0000u) * (__uint_as_float(dr[c4 + 3]) - dl.w);
+          pk[col / 2] = pack_bf16x2(e0, e1);
+          pk[col / 2 + 1] = pack_bf16x2(e2, e3);
         }
       }
+      tc_fence_before();
       // dV has consumed P^T: overwrite the tile with dS^T
       ok = mbar_wait(bDV, it & 1, abort_flag, kSiteBwdMma);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
 #pragma unroll
       for (int ch = 0; ch < BM / 8; ++ch) {
-        *reinterpret_cast<uint4*>(prow_base + sw128_offset(r, ch, BN)) =
+        *reinterpret_cast<uint4*>(sP + sw128_offset(r, ch, BN)) =
             make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
       }
       fence_proxy_async_smem();
       mbar_arrive(bDS);
-
-      // drain dQ_i (TMEM lane = query row) into the fp32 accumulator
-      ok = mbar_wait(bDQf, it & 1, abort_flag, kSiteBwdMma);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      {
-        const int qi = q0 + r;
-        float* dst = p.dq_acc + ((size_t)bh * p.Nq + qi) * D;
-        uint32_t qr[32];
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tmem_ld32(tmem + lane_base + kColS + c * 32, qr);
-          tmem_wait_ld();
-          if (qi < p.Nq) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              red_add_v4(dst + c * 32 + i, __uint_as_float(qr[i]), __uint_as_float(qr[i + 1]),
-                         __uint_as_float(qr[i + 2]), __uint_as_float(qr[i + 3]));
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(bDQfree);
     }
     // epilogue: dV, dK rows of this key tile (TMEM loads are warp-wide;
     // only rows inside the sequence are stored)
+    if (ok && n_it > 0) {
+      ok = mbar_wait(bFinal, 0, abort_flag, kSiteBwdMma);
+      ok = __all_sync(0xffffffffu, ok);
+    }
     if (ok) {
       const bool store = kv_idx < p.Nkv;
       __nv_bfloat16* dvrow = p.dv + ((size_t)bh * p.Nkv + kv_idx) * D;
       __nv_bfloat16* dkrow = p.dk + ((size_t)bh * p.Nkv + kv_idx) * D;
       if (n_it > 0) {
         tc_fence_after();
-        uint32_t rr[32];
+#pragma unroll 1
+        for (int which = 0; which < 2; ++which) {
+          const uint32_t col0 = which ? kColDK : kColDV;
+          const float sc = which ? p.scale : 1.f;
+          __nv_bfloat16* rowp = which ? dkrow : dvrow;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t rr[32];
+            tmem_ld32(tmem + lane_base + col0 + c * 32, rr);
+            tmem_wait_ld();
+            reg_fence(rr);
+            uint32_t w[16];
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tmem_ld32(tmem + lane_base + kColDV + c * 32, rr);
-          tmem_wait_ld();
-          uint32_t w[16];
+            for (int i = 0; i < 16; ++i)
+              w[i] = pack_bf16x2(__uint_as_float(rr[2 * i]) * sc, __uint_as_float(rr[2 * i + 1]) * sc);
+            uint4* dst = reinterpret_cast<uint4*>(rowp + c * 32);
+            if (store) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1]));
-          uint4* dst = reinterpret_cast<uint4*>(dvrow + c * 32);
-          if (store) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tmem_ld32(tmem + lane_base + kColDK + c * 32, rr);
-          tmem_wait_ld();
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pack_bf16x2(__uint_as_float(rr[2 * i]) * p.scale, __uint_as_float(rr[2 * i + 1]) * p.scale);
-          uint4* dst = reinterpret_cast<uint4*>(dkrow + c * 32);
-          if (store) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+              for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            }
           }
         }
       } else if (store) {
@@ -427,11 +423,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else {
+    // ---------------- dQ drain warps 4-7 ----------------
+    // warp w reads TMEM lanes 32*(w%4).. : query rows qr0 .. qr0+31 of dQ_it
+    const int qr0 = (warp & 3) * 32;
+    const uint32_t lane_base = static_cast<uint32_t>(qr0) << 16;
+    // this warp's two 4 KB staging buffers (32 rows x 32 fp32, 128-byte swizzle)
+    uint8_t* stage = sP + (warp & 3) * 8192;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = (first_q + it) * BM;
+      ok = mbar_wait(bDQf, it & 1, abort_flag, kSiteBwdDq);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      // dQ_it's MMAs have completed, so the P^T/dS^T tile is free for staging.
+      // Two halves of 64 columns (bounded registers); dP's columns are released
+      // as soon as the second half is in registers.
+#pragma unroll
+      for (int h = 0; h < D / 64; ++h) {
+        uint32_t qh[64];
+        tmem_ld32(tmem + lane_base + kColDP + h * 64, *reinterpret_cast<uint32_t(*)[32]>(qh));
+        tmem_ld32(tmem + lane_base + kColDP + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(qh + 32));
+        tmem_wait_ld();
+        reg_fence(qh);
+        if (h == D / 64 - 1) {
+          tc_fence_before();
+          mbar_arrive(bDQfree);        // dP's columns are free for dP^T of the next tile
+        }
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = h * 2 + cc;     // 32-column chunk
+          uint8_t* buf = stage + (c & 1) * 4096;
+          if (c >= 2) {                 // buffer reuse: its previous reduction must have read it
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+                make_uint4(qh[cc * 32 + 4 * k], qh[cc * 32 + 4 * k + 1], qh[cc * 32 + 4 * k + 2],
+                           qh[cc * 32 + 4 * k + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_3d(&tmDQ, buf, c * 32, q0 + qr0, bh);
+            bulk_commit_group();
+          }
+        }
+      }
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bPfree);
+    }
+    if (lane == 0) bulk_wait_group<0>();   // reductions complete before exit
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -522,11 +573,12 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
     int rc = check_cuda(cudaGetLastError(), "backward prep launch");
     if (rc) return rc;
   }
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   int rc = make_tmap_bf16_3d(&tq, q, D, Nq, BH, 64, BM, true);
   if (!rc) rc = make_tmap_bf16_3d(&tk, k, D, Nkv, BH, 64, BN, true);
   if (!rc) rc = make_tmap_bf16_3d(&tv, v, D, Nkv, BH, 64, BN, true);
   if (!rc) rc = make_tmap_bf16_3d(&tdo, dout, D, Nq, BH, 64, BM, true);
+  if (!rc) rc = make_tmap_f32_3d(&tdq, dq_acc, D, Nq, BH, 32, 32, true);
   if (rc) return rc;
   static bool attr_done[64] = {false};
   const int dev = current_device();
@@ -549,13 +601,12 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
   prm.nq_pad = (int)nq_pad;
   prm.lse2 = lse2;
   prm.delta = delta;
-  prm.dq_acc = dq_acc;
   prm.dk = static_cast<__nv_bfloat16*>(dk);
   prm.dv = static_cast<__nv_bfloat16*>(dv);
   const long long n_kv_tiles = (Nkv + BN - 1) / BN;
   if (BH > 65535) return set_error(PU_ERR_UNSUPPORTED, "B*H = %lld exceeds 65535", BH);
   dim3 grid((unsigned)n_kv_tiles, (unsigned)BH);
-  attn_bwd_kernel<D><<<grid, kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, prm);
+  attn_bwd_kernel<D><<<grid, kThreads, C::kSmemBytes, st>>>(tq, tk, tv, tdo, tdq, prm);
   rc = check_cuda(cudaGetLastError(), "backward main launch");
   if (rc) return rc;
   const long long n8 = BH * Nq * D / 8;
