@@ -21,16 +21,17 @@
 //              dS^T = P^T (dP^T - Delta)                  (bf16, over P^T)
 //              dK  += dS^T Q     -> TMEM [384,384+D)
 //              dQ_i = dS K       -> TMEM [128,128+D) (dP^T's columns)
-//            S^T of the next query tile is issued right after dQ_i, so the
-//            tensor core works on it while dQ_i is drained.
 //   post   : dQ = bf16(scale * dQ accumulator).
 // Warp roles of the main kernel:
-//   warps 0-3  P^T and dS^T (thread r = key row r), then the dK/dV epilogue.
-//   warps 4-7  dQ drain: each warp takes 32 query rows of dQ_i from TMEM,
-//              stages 32x32 fp32 chunks (128-byte swizzle) in the P^T/dS^T
-//              tile once the MMAs have read it, and adds them into the fp32
-//              accumulator with TMA bulk tensor reductions.
+//   warps 0-7  two warpgroups, each owning 64 of the 128 query columns: P^T
+//              and dS^T for every key row (thread = TMEM lane = key row), the
+//              drain of dQ_i (thread = lane = query row): 32x32 fp32 chunks
+//              staged with 128-byte swizzle in dO_i's consumed slot and added
+//              into the fp32 accumulator with TMA bulk tensor reductions; and
+//              their half of the dK/dV epilogue.
 //   warp 8     TMA producer.   warp 9  tcgen05 issuer + TMEM owner.
+// Tensor-core order per query tile i: dP_i, dV_i, S_{i+1}, dK_i, dQ_i — so
+// S_{i+1} is ready when the warpgroups finish dS_i.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -53,19 +54,22 @@ struct Cfg {
   static constexpr int NSQ = 2;                  // Q / dO ring depth
   static constexpr int kTileQ = BM * D * 2;
   static constexpr int kTileKV = BN * D * 2;
-  static constexpr int kTileP = BN * BM * 2;     // P^T / dS^T, bf16 [BN][BM]; dQ staging
+  static constexpr int kTileP = BN * BM * 2;     // P^T / dS^T, bf16 [BN][BM]
+  static constexpr int kStageBytes = 8 * 4096;   // dQ staging: 4 KB per compute warp
+  // D = 128: the consumed dO slot (32 KB) stages dQ; D = 64: a dedicated buffer
+  static constexpr bool kStageInDO = (kTileQ >= kStageBytes);
   static constexpr int kColBlocks = D / 64;
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kTileKV;
   static constexpr int kOffQ = kOffV + kTileKV;
   static constexpr int kOffDO = kOffQ + NSQ * kTileQ;
   static constexpr int kOffP = kOffDO + NSQ * kTileQ;
-  static constexpr int kOffStats = kOffP + kTileP;          // [NSQ][lse_log2[BM], delta[BM]]
+  static constexpr int kOffStage = kOffP + kTileP;
+  static constexpr int kOffStats = kOffStage + (kStageInDO ? 0 : kStageBytes);  // [NSQ][lse2[BM], delta[BM]]
   static constexpr int kStatBytes = 2 * BM * 4;
   static constexpr int kOffBar = kOffStats + NSQ * kStatBytes;
-  // barriers: KV, Qf[NSQ], Qe[NSQ], dOf[NSQ], dOe[NSQ], S, dP, P, dV, dS, dQf,
-  //           dQfree, PdSfree, final
-  static constexpr int kNumBars = 1 + 4 * NSQ + 10;
+  // barriers: KV, Qf[NSQ], Qe[NSQ], dOf[NSQ], dOe[NSQ], S, dP, P, dV, dS, dQf, dQfree, final
+  static constexpr int kNumBars = 1 + 4 * NSQ + 8;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -98,6 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const __grid_constant__ CUtensorMap tmDQ, const Params p) {
   using C = Cfg<D>;
+  constexpr int HC = BM / 2;               // query columns per compute warpgroup
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -125,8 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bDS = bDV + 1;
   uint64_t* bDQf = bDS + 1;
   uint64_t* bDQfree = bDQf + 1;
-  uint64_t* bPfree = bDQfree + 1;
-  uint64_t* bFinal = bPfree + 1;
+  uint64_t* bFinal = bDQfree + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bFinal + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -145,16 +149,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bQf + s, 1);
       mbar_init(bQe + s, 1);
       mbar_init(bDOf + s, 1);
-      mbar_init(bDOe + s, 1);
+      mbar_init(bDOe + s, 8);    // released by the 8 dQ-staging warps
     }
     mbar_init(bS, 1);
     mbar_init(bDP, 1);
-    mbar_init(bP, 128);
+    mbar_init(bP, 256);
     mbar_init(bDV, 1);
-    mbar_init(bDS, 128);
+    mbar_init(bDS, 256);
     mbar_init(bDQf, 1);
-    mbar_init(bDQfree, 128);
-    mbar_init(bPfree, 4);
+    mbar_init(bDQfree, 256);
     mbar_init(bFinal, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -247,7 +250,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                  make_sdesc_sw128(aDO + kk * 16 * 128, BM * 128, 1024), idKMN, (it > 0 || kk > 0));
         }
         mma_commit(bDV);
-        mma_commit(bDOe + st);
+        // next query tile's S^T: S's columns were read before P^T was published
+        if (it + 1 < n_it) {
+          if (!mbar_wait(bQf + (it + 1) % C::NSQ, ((it + 1) / C::NSQ) & 1, abort_flag, kSiteBwdLoad)) break;
+          tc_fence_after();
+          issue_S(it + 1);
+        }
         // dK += dS^T Q ; dQ_it = dS K (into dP's columns)
         if (!mbar_wait(bDS, it & 1, abort_flag, kSiteBwdDs)) break;
         tc_fence_after();
@@ -264,23 +272,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bDQf);
         mma_commit(bQe + st);
-        // next query tile's S^T (S columns were read before P^T was published)
-        if (it + 1 < n_it) {
-          const int nst = (it + 1) % C::NSQ;
-          if (!mbar_wait(bQf + nst, ((it + 1) / C::NSQ) & 1, abort_flag, kSiteBwdLoad)) break;
-          tc_fence_after();
-          issue_S(it + 1);
-        } else {
-          mma_commit(bFinal);
-        }
+        if (it + 1 == n_it) mma_commit(bFinal);
       }
     }
-  } else if (warp < 4) {
-    // ---------------- P^T / dS^T warps 0-3, then the dK/dV epilogue ----------------
-    const int r = tid;                                    // key row within the tile
+  } else {
+    // ---------------- compute warps 0-7 ----------------
+    // Warpgroup g (warps 4g..4g+3) owns query columns [64g, 64g+64) of P^T,
+    // dS^T and dQ; warp w reads TMEM lanes 32*(w%4).. (key rows for S^T/dP^T,
+    // query rows for dQ).
+    const int g = warp >> 2;
+    const int r = tid & 127;                              // TMEM lane
     const int kv_idx = kv0 + r;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int cbase = g * HC;                             // first query column of this warpgroup
     bool ok = true;
+
+    // Drain dQ_j (this warpgroup's 64 columns of the rows in this warp's
+    // lanes) into the fp32 accumulator: TMEM -> registers (then dP's columns
+    // are released) -> 4 KB swizzled staging per 32x32 chunk -> TMA reduce-add.
+    auto drain = [&](int j) -> bool {
+      constexpr int DQC = D / 2;                      // dQ columns per warpgroup
+      bool okd = mbar_wait(bDQf, j & 1, abort_flag, kSiteBwdDq);
+      okd = __all_sync(0xffffffffu, okd);
+      if (!okd) return false;
+      tc_fence_after();
+      uint32_t qh[DQC];
+#pragma unroll
+      for (int c = 0; c < DQC / 32; ++c)
+        tmem_ld32(tmem + lane_base + kColDP + g * DQC + c * 32, *reinterpret_cast<uint32_t(*)[32]>(qh + c * 32));
+      tmem_wait_ld();
+      reg_fence(qh);
+      tc_fence_before();
+      mbar_arrive(bDQfree);
+      const int q0j = (first_q + j) * BM;
+      uint8_t* buf = (C::kStageInDO ? sDO + (j % C::NSQ) * C::kTileQ : smem + C::kOffStage) + warp * 4096;
+#pragma unroll
+      for (int c = 0; c < DQC / 32; ++c) {
+        if (c > 0) {                    // single buffer: the previous reduction must have read it
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          *reinterpret_cast<uint4*>(buf + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+              make_uint4(qh[c * 32 + 4 * k], qh[c * 32 + 4 * k + 1], qh[c * 32 + 4 * k + 2],
+                         qh[c * 32 + 4 * k + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&tmDQ, buf, g * DQC + c * 32, q0j + (warp & 3) * 32, bh);
+          bulk_commit_group();
+        }
+      }
+      if (lane == 0) {
+        bulk_wait_group_read<0>();
+        mbar_arrive(bDOe + (j % C::NSQ));   // the staging (dO_j's slot) may be refilled
+      }
+      __syncwarp();
+      return true;
+    };
+
     for (int it = 0; it < n_it; ++it) {
       const int q0 = (first_q + it) * BM;
       const int st = it % C::NSQ;
@@ -288,54 +340,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(bQf + st, (it / C::NSQ) & 1, abort_flag, kSiteBwdLoad);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      const float* lse_t = s_stats + st * 2 * BM;
-      const float* del_t = lse_t + BM;
+      const float* lse_t = s_stats + st * 2 * BM + cbase;
+      const float* del_t = s_stats + st * 2 * BM + BM + cbase;
 
       ok = mbar_wait(bS, it & 1, abort_flag, kSiteBwdMma);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t pk[BM / 2];
+      uint32_t pk[HC / 2];
       {
-        const bool need_mask = (p.causal && q0 < kv0 + BN - 1) || (q0 + BM > p.Nq) || (kv_idx >= p.Nkv);
+        uint32_t sr[HC];
+        tmem_ld32(tmem + lane_base + kColS + cbase, *reinterpret_cast<uint32_t(*)[32]>(sr));
+        tmem_ld32(tmem + lane_base + kColS + cbase + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+        tmem_wait_ld();
+        reg_fence(sr);
+        const int qb = q0 + cbase;
+        const bool need_mask = (p.causal && qb < kv0 + BN - 1) || (qb + HC > p.Nq) || (kv_idx >= p.Nkv);
         const int lo = p.causal ? kv_idx : 0;     // key kv_idx is visible to queries >= lo
         const bool kv_ok = kv_idx < p.Nkv;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {           // two halves of 64 columns: bounded registers
-          uint32_t sr[64];
-          tmem_ld32(tmem + lane_base + kColS + h * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
-          tmem_ld32(tmem + lane_base + kColS + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-          tmem_wait_ld();
-          reg_fence(sr);
-#pragma unroll
-          for (int c4 = 0; c4 < 64; c4 += 4) {
-            const int col = h * 64 + c4;
-            const float4 lv = *reinterpret_cast<const float4*>(lse_t + col);
-            float p0 = ex2(fmaf(__uint_as_float(sr[c4]), p.scale_log2, -lv.x));
-            float p1 = ex2(fmaf(__uint_as_float(sr[c4 + 1]), p.scale_log2, -lv.y));
-            float p2 = ex2(fmaf(__uint_as_float(sr[c4 + 2]), p.scale_log2, -lv.z));
-            float p3 = ex2(fmaf(__uint_as_float(sr[c4 + 3]), p.scale_log2, -lv.w));
-            if (need_mask) {
-              const int qa = q0 + col;
-              if (!(kv_ok && qa >= lo && qa < p.Nq)) p0 = 0.f;
-              if (!(kv_ok && qa + 1 >= lo && qa + 1 < p.Nq)) p1 = 0.f;
-              if (!(kv_ok && qa + 2 >= lo && qa + 2 < p.Nq)) p2 = 0.f;
-              if (!(kv_ok && qa + 3 >= lo && qa + 3 < p.Nq)) p3 = 0.f;
-            }
-            pk[col / 2] = pack_bf16x2(p0, p1);
-            pk[col / 2 + 1] = pack_bf16x2(p2, p3);
+        for (int c4 = 0; c4 < HC; c4 += 4) {
+          const float4 lv = *reinterpret_cast<const float4*>(lse_t + c4);
+          float p0 = ex2(fmaf(__uint_as_float(sr[c4]), p.scale_log2, -lv.x));
+          float p1 = ex2(fmaf(__uint_as_float(sr[c4 + 1]), p.scale_log2, -lv.y));
+          float p2 = ex2(fmaf(__uint_as_float(sr[c4 + 2]), p.scale_log2, -lv.z));
+          float p3 = ex2(fmaf(__uint_as_float(sr[c4 + 3]), p.scale_log2, -lv.w));
+          if (need_mask) {
+            const int qa = qb + c4;
+            if (!(kv_ok && qa >= lo && qa < p.Nq)) p0 = 0.f;
+            if (!(kv_ok && qa + 1 >= lo && qa + 1 < p.Nq)) p1 = 0.f;
+            if (!(kv_ok && qa + 2 >= lo && qa + 2 < p.Nq)) p2 = 0.f;
+            if (!(kv_ok && qa + 3 >= lo && qa + 3 < p.Nq)) p3 = 0.f;
           }
+          pk[c4 / 2] = pack_bf16x2(p0, p1);
+          pk[c4 / 2 + 1] = pack_bf16x2(p2, p3);
         }
       }
-      // the drain of dQ_{it-1} must have finished reading its staging from the tile
+      // dQ_{it-1}: its MMAs completing also frees the P^T/dS^T tile
       if (it > 0) {
-        ok = mbar_wait(bPfree, (it - 1) & 1, abort_flag, kSiteBwdDs);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = drain(it - 1);
         if (!ok) break;
       }
 #pragma unroll
-      for (int ch = 0; ch < BM / 8; ++ch) {
-        *reinterpret_cast<uint4*>(sP + sw128_offset(r, ch, BN)) =
+      for (int ch = 0; ch < HC / 8; ++ch) {
+        *reinterpret_cast<uint4*>(sP + sw128_offset(r, g * 8 + ch, BN)) =
             make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
       }
       fence_proxy_async_smem();
@@ -346,24 +394,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t dr[64];
-        tmem_ld32(tmem + lane_base + kColDP + h * 64, *reinterpret_cast<uint32_t(*)[32]>(dr));
-        tmem_ld32(tmem + lane_base + kColDP + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
+      {
+        uint32_t dr[HC];
+        tmem_ld32(tmem + lane_base + kColDP + cbase, *reinterpret_cast<uint32_t(*)[32]>(dr));
+        tmem_ld32(tmem + lane_base + kColDP + cbase + 32, *reinterpret_cast<uint32_t(*)[32]>(dr + 32));
         tmem_wait_ld();
         reg_fence(dr);
 #pragma unroll
-        for (int c4 = 0; c4 < 64; c4 += 4) {
-          const int col = h * 64 + c4;
-          const float4 dl = *reinterpret_cast<const float4*>(del_t + col);
-          const uint32_t pa = pk[col / 2], pb = pk[col / 2 + 1];
+        for (int c4 = 0; c4 < HC; c4 += 4) {
+          const float4 dl = *reinterpret_cast<const float4*>(del_t + c4);
+          const uint32_t pa = pk[c4 / 2], pb = pk[c4 / 2 + 1];
           const float e0 = __uint_as_float(pa << 16) * (__uint_as_float(dr[c4]) - dl.x);
           const float e1 = __uint_as_float(pa & 0xFFFF0000u) * (__uint_as_float(dr[c4 + 1]) - dl.y);
           const float e2 = __uint_as_float(pb << 16) * (__uint_as_float(dr[c4 + 2]) - dl.z);
           const float e3 = __uint_as_float(pb & 0xFFFF0000u) * (__uint_as_float(dr[c4 + 3]) - dl.w);
-          pk[col / 2] = pack_bf16x2(e0, e1);
-          pk[col / 2 + 1] = pack_bf16x2(e2, e3);
+          pk[c4 / 2] = pack_bf16x2(e0, e1);
+          pk[c4 / 2 + 1] = pack_bf16x2(e2, e3);
         }
       }
       tc_fence_before();
@@ -372,32 +418,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
 #pragma unroll
-      for (int ch = 0; ch < BM / 8; ++ch) {
-        *reinterpret_cast<uint4*>(sP + sw128_offset(r, ch, BN)) =
+      for (int ch = 0; ch < HC / 8; ++ch) {
+        *reinterpret_cast<uint4*>(sP + sw128_offset(r, g * 8 + ch, BN)) =
             make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
       }
       fence_proxy_async_smem();
       mbar_arrive(bDS);
     }
-    // epilogue: dV, dK rows of this key tile (TMEM loads are warp-wide;
-    // only rows inside the sequence are stored)
+    if (ok && n_it > 0) ok = drain(n_it - 1);
+    // epilogue: this warpgroup's 64 columns of dV, dK for the key rows in this
+    // warp's lanes (TMEM loads are warp-wide; only rows inside the sequence
+    // are stored)
     if (ok && n_it > 0) {
       ok = mbar_wait(bFinal, 0, abort_flag, kSiteBwdMma);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
       const bool store = kv_idx < p.Nkv;
-      __nv_bfloat16* dvrow = p.dv + ((size_t)bh * p.Nkv + kv_idx) * D;
-      __nv_bfloat16* dkrow = p.dk + ((size_t)bh * p.Nkv + kv_idx) * D;
+      constexpr int DC = D / 2;                 // dV/dK columns per warpgroup
+      __nv_bfloat16* dvrow = p.dv + ((size_t)bh * p.Nkv + kv_idx) * D + g * DC;
+      __nv_bfloat16* dkrow = p.dk + ((size_t)bh * p.Nkv + kv_idx) * D + g * DC;
       if (n_it > 0) {
         tc_fence_after();
 #pragma unroll 1
         for (int which = 0; which < 2; ++which) {
-          const uint32_t col0 = which ? kColDK : kColDV;
+          const uint32_t col0 = (which ? kColDK : kColDV) + g * DC;
           const float sc = which ? p.scale : 1.f;
           __nv_bfloat16* rowp = which ? dkrow : dvrow;
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < DC / 32; ++c) {
             uint32_t rr[32];
             tmem_ld32(tmem + lane_base + col0 + c * 32, rr);
             tmem_wait_ld();
@@ -417,67 +466,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // no query attends to these keys: zero gradients
         const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int i = 0; i < D / 8; ++i) {
+        for (int i = 0; i < DC / 8; ++i) {
           reinterpret_cast<uint4*>(dvrow)[i] = z;
           reinterpret_cast<uint4*>(dkrow)[i] = z;
         }
       }
     }
-  } else {
-    // ---------------- dQ drain warps 4-7 ----------------
-    // warp w reads TMEM lanes 32*(w%4).. : query rows qr0 .. qr0+31 of dQ_it
-    const int qr0 = (warp & 3) * 32;
-    const uint32_t lane_base = static_cast<uint32_t>(qr0) << 16;
-    // this warp's two 4 KB staging buffers (32 rows x 32 fp32, 128-byte swizzle)
-    uint8_t* stage = sP + (warp & 3) * 8192;
-    bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int q0 = (first_q + it) * BM;
-      ok = mbar_wait(bDQf, it & 1, abort_flag, kSiteBwdDq);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      // dQ_it's MMAs have completed, so the P^T/dS^T tile is free for staging.
-      // Two halves of 64 columns (bounded registers); dP's columns are released
-      // as soon as the second half is in registers.
-#pragma unroll
-      for (int h = 0; h < D / 64; ++h) {
-        uint32_t qh[64];
-        tmem_ld32(tmem + lane_base + kColDP + h * 64, *reinterpret_cast<uint32_t(*)[32]>(qh));
-        tmem_ld32(tmem + lane_base + kColDP + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(qh + 32));
-        tmem_wait_ld();
-        reg_fence(qh);
-        if (h == D / 64 - 1) {
-          tc_fence_before();
-          mbar_arrive(bDQfree);        // dP's columns are free for dP^T of the next tile
-        }
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = h * 2 + cc;     // 32-column chunk
-          uint8_t* buf = stage + (c & 1) * 4096;
-          if (c >= 2) {                 // buffer reuse: its previous reduction must have read it
-            if (lane == 0) bulk_wait_group_read<1>();
-            __syncwarp();
-          }
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            *reinterpret_cast<uint4*>(buf + lane * 128 + ((k ^ (lane & 7)) << 4)) =
-                make_uint4(qh[cc * 32 + 4 * k], qh[cc * 32 + 4 * k + 1], qh[cc * 32 + 4 * k + 2],
-                           qh[cc * 32 + 4 * k + 3]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_reduce_add_3d(&tmDQ, buf, c * 32, q0 + qr0, bh);
-            bulk_commit_group();
-          }
-        }
-      }
-      if (lane == 0) bulk_wait_group_read<0>();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bPfree);
-    }
-    if (lane == 0) bulk_wait_group<0>();   // reductions complete before exit
+    if (lane == 0) bulk_wait_group<0>();   // dQ reductions complete before exit
   }
 
   tc_fence_before();
