@@ -169,24 +169,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idS = make_idesc_bf16(BM, BN, 0, 0);
       constexpr uint32_t idO = make_idesc_bf16(BM, D, 0, 1);
+      // descriptors are built once; per MMA only the start address moves
+      const uint64_t dQ0 = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t dK0 = make_sdesc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t dV0 = make_sdesc_sw128(smem_u32(sV), BN * 128, 1024);
       auto issue_S = [&](int t, int j) {
-        const uint32_t aQ = smem_u32(sQ + t * C::kTileQ);
-        const uint32_t aK = smem_u32(sK + (j % C::NS) * C::kTileKV);
+        const uint64_t dq = sdesc_add(dQ0, t * C::kTileQ);
+        const uint64_t dk = sdesc_add(dK0, (j % C::NS) * C::kTileKV);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint32_t offk = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          mma_ss(tmem + col_s(t), make_sdesc_sw128(aQ + off, 16, 1024),
-                 make_sdesc_sw128(aK + offk, 16, 1024), idS, kk > 0);
+          mma_ss(tmem + col_s(t), sdesc_add(dq, off), sdesc_add(dk, offk), idS, kk > 0);
         }
         mma_commit(bS + t);
       };
       auto issue_PV = [&](int t, int j) {
-        const uint32_t aV = smem_u32(sV + (j % C::NS) * C::kTileKV);
+        const uint64_t dv = sdesc_add(dV0, (j % C::NS) * C::kTileKV);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          mma_ts(tmem + col_o(t), tmem + col_s(t) + kk * 8,
-                 make_sdesc_sw128(aV + kk * 16 * 128, BN * 128, 1024), idO, (j > 0 || kk > 0));
+          mma_ts(tmem + col_o(t), tmem + col_s(t) + kk * 8, sdesc_add(dv, kk * 16 * 128), idO,
+                 (j > 0 || kk > 0));
         }
       };
       bool ok = mbar_wait(bKf, 0, abort_flag, kSiteFwdKFull);

@@ -95,6 +95,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int where) {
   const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;   // common case: already complete
 #pragma unroll 1
   for (int i = 0; i < 256; ++i) {
     if (mbar_try_wait(addr, parity)) return true;
@@ -349,6 +350,12 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_
   d |= static_cast<uint64_t>(1) << 46;
   d |= static_cast<uint64_t>(2) << 61;
   return d;
+}
+
+// Advance a shared-memory descriptor's start address by `bytes` (a multiple
+// of 16; the sum stays below 256 KB, so only the address field changes).
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t bytes) {
+  return desc + static_cast<uint64_t>(bytes >> 4);
 }
 
 // Instruction descriptor for kind::f16 with bf16 inputs, fp32 accumulate:
