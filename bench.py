@@ -41,6 +41,13 @@ DEC_B, DEC_H, DEC_N, DEC_D = 1, 32, 32768, 128
 FWD_FLOPS = 4 * B * H * N * N * D * 0.5          # causal
 STEP_FLOPS = FWD_FLOPS * 3.5                      # fwd + 2.5x bwd
 L2_BYTES = 126 * 1024 * 1024
+# DRAM bytes (read + write) per launch from one ncu capture of this workload
+# (see the summaries under profiles/); re-measured whenever a kernel changes.
+NCU_TRAFFIC_BYTES = {
+    "attn_fwd": 201_384_192 + 50_688_512,
+    "attn_bwd": (270_716_160 + 109_300_480) + (270_625_280 + 52_647_680) + 135_000_000,
+    "split_kv": 536_905_728 + 3_892_736,
+}
 
 
 def load_peaks() -> dict:
@@ -368,11 +375,13 @@ def main():
     if rank == 0:
         bwd_flops = FWD_FLOPS * 2.5
         achieved = bwd_flops / (bwd_ms_max * 1e-3) / 1e12
-        roof = {"kernel": "attn_bwd (prep + tcgen05 main + dq post, one pu_attn_bwd call)",
+        roof = {"kernel": "attn_bwd (prep + dK/dV + dQ kernels, one pu_attn_bwd call)",
                 "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                 "peak_source": peaks["source"] + " bf16 burst",
-                "traffic": None}
+                "traffic": NCU_TRAFFIC_BYTES["attn_bwd"],
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, "
+                                  "profiles/attn_bwd_*_causal_B4H16N4096D128.md"}
         fwd_ach = FWD_FLOPS / (fwd_ms_max * 1e-3) / 1e12
         cpu = None
         if world == 1:
@@ -400,7 +409,8 @@ def main():
                        "l2": "inputs 268 MB per GPU > 126 MB L2 (no flush needed)"},
             "roofline": roof,
             "roofline_fwd": {"kernel": "attn_fwd", "achieved": round(fwd_ach, 1),
-                             "frac": round(fwd_ach / peaks["bf16_tflops"], 4), "unit": "TFLOP/s"},
+                             "frac": round(fwd_ach / peaks["bf16_tflops"], 4), "unit": "TFLOP/s",
+                             "traffic": NCU_TRAFFIC_BYTES["attn_fwd"]},
             "cpu_baseline": cpu,
             "e2e": {"value": round(STEP_FLOPS * world / e2e_dt / 1e12, 3), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -415,7 +425,8 @@ def main():
                        "kernel_us": round(dec_kus, 2),
                        "roofline": {"bound": "hbm", "achieved": round(dec_bytes / (dec_kus * 1e-6) / 1e9, 1),
                                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                                    "frac": round(dec_bytes / (dec_kus * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)},
+                                    "frac": round(dec_bytes / (dec_kus * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
+                                    "traffic": NCU_TRAFFIC_BYTES["split_kv"] if world == 1 else None},
                        "l2": "256 MB buffer written before every step"},
         }
         if world == 1:

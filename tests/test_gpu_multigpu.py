@@ -1,0 +1,99 @@
+"""Multi-GPU paths on real GPUs (skipped with fewer than 2 devices).
+
+* Sequence-sharded split-KV decode: each rank holds a contiguous chunk of
+  the KV cache, runs pu_decode_partial, the packed (m, l, o) partials move
+  with one NCCL all-gather, and pu_decode_combine merges them; every rank
+  must match the oracle's whole-cache decode.
+* Head-partitioned training attention: each rank runs forward + backward
+  on its heads only (no collective); the gathered outputs match the oracle.
+Runs world_size 2 as spawned processes with NCCL_NVLS_ENABLE=0.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+for p in (str(ROOT), str(ROOT / "pallas-unbound_b200"), str(ROOT / "tests")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+pytestmark = pytest.mark.gpu
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from helpers import randn
+    from oracle import attention as orc
+    from pallas_flash.kernels.decoding import pallas_flash_decoding
+    from pallas_flash.ops.interface import flash_attention_backward, flash_attention_forward
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    res = {}
+    # --- sequence-sharded decode ---
+    B, H, N, D = 2, 8, 8192, 128
+    q = randn((B, H, 1, D), 71, dtype=torch.float16)
+    k = randn((B, H, N, D), 72, dtype=torch.float16)
+    v = randn((B, H, N, D), 73, dtype=torch.float16)
+    lens = torch.tensor([N, 5000], dtype=torch.int32)
+    n = N // world
+    ks = k[:, :, rank * n:(rank + 1) * n].contiguous().cuda()
+    vs = v[:, :, rank * n:(rank + 1) * n].contiguous().cuda()
+    o, lse = pallas_flash_decoding(q.cuda(), ks, vs, kv_lens=lens.cuda(), group=dist.group.WORLD,
+                                   return_lse=True)
+    ro, rl = orc.decode_forward(q.float().numpy(), k.float().numpy(), v.float().numpy(), kv_lens=lens.numpy())
+    res["dec_o"] = orc.compare(o.float().cpu().numpy(), ro)
+    res["dec_lse"] = orc.compare(lse.cpu().numpy(), rl)
+    # --- head-partitioned training attention ---
+    B, H, N, D = 1, 4, 512, 128
+    qg, kg, vg, dog = (randn((B, H, N, D), 80 + i) for i in range(4))
+    hs = H // world
+    sl = slice(rank * hs, (rank + 1) * hs)
+    ql, kl, vl, dol = (t[:, sl].contiguous().cuda() for t in (qg, kg, vg, dog))
+    ol, lsel = flash_attention_forward(ql, kl, vl, causal=True)
+    dql, dkl, dvl = flash_attention_backward(ql, kl, vl, ol, lsel, dol, causal=True)
+    f = lambda t: t.float().numpy()
+    ro, rl = orc.mha_forward(f(qg)[:, sl], f(kg)[:, sl], f(vg)[:, sl], causal=True)
+    rdq, rdk, rdv = orc.mha_backward(f(qg)[:, sl], f(kg)[:, sl], f(vg)[:, sl], ro, rl, f(dog)[:, sl], causal=True)
+    res["tr_o"] = orc.compare(ol.float().cpu().numpy(), ro)
+    for name, got, ref in (("dq", dql, rdq), ("dk", dkl, rdk), ("dv", dvl, rdv)):
+        res["tr_" + name] = orc.compare(got.float().cpu().numpy(), ref)
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+    import json
+    Path(out_dir, f"rank{rank}.json").write_text(json.dumps(res))
+
+
+def test_two_gpu_decode_and_partitioned_training(tmp_path, built_lib):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import json
+    import torch.multiprocessing as mp
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    mp.start_processes(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    for rank in range(2):
+        res = json.loads(Path(tmp_path, f"rank{rank}.json").read_text())
+        assert res["dec_o"]["max_abs"] <= 2e-2 and res["dec_o"]["rel"] <= 1e-2, res
+        assert res["dec_lse"]["max_abs"] <= 1e-3, res
+        assert res["tr_o"]["max_abs"] <= 2e-2 and res["tr_o"]["rel"] <= 1e-2, res
+        for g in ("dq", "dk", "dv"):
+            assert res["tr_" + g]["rel"] <= 3e-2, res
