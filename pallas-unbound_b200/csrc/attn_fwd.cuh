@@ -21,8 +21,9 @@
 //               units; the running max only moves (O and l rescaled) when it
 //               grows by more than kRescaleLog2, so P <= 2^8.  P is written
 //               as bf16 over the first 64 columns of the tile's S columns.
-//               Partial maxima / sums in 8 independent accumulators keep the
-//               reductions from serialising on instruction latency.
+//               Partial maxima in 8 independent accumulators and the row
+//               sum in packed f32x2 pairs keep the reductions from
+//               serialising on instruction latency.
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
 // Ordering: the commit that signals S_t(j+1) also covers O_t += P_t(j) V_j
 // (issued earlier by the same thread), so a softmax warpgroup that has seen
@@ -293,25 +294,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(tO + c * 32, r);
         }
       }
-      const float neg_m = -m_ref;
-      float rs8[8];
+      // P = 2^(s*scale - m): scale-subtract and row sum on pairs of scores in
+      // packed f32x2 arithmetic (half the instructions), exp2 on MUFU
+      const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+      const uint64_t negm2 = f2_pack(-m_ref, -m_ref);
+      uint64_t rs2[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
+      for (int i = 0; i < 4; ++i) rs2[i] = 0ull;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int c = h * 64 + 2 * i;
-          const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, neg_m));
-          const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, neg_m));
-          rs8[(2 * i) & 7] += p0;
-          rs8[(2 * i + 1) & 7] += p1;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), scale2, negm2), x0, x1);
+          const float p0 = ex2(x0);
+          const float p1 = ex2(x1);
+          rs2[i & 3] = f2_add(rs2[i & 3], f2_pack(p0, p1));
           pk[i] = pack_bf16x2(p0, p1);
         }
         tmem_st32(tS + h * 32, pk);
       }
-      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      float ra, rb, rc, rd;
+      f2_unpack(f2_add(rs2[0], rs2[1]), ra, rb);
+      f2_unpack(f2_add(rs2[2], rs2[3]), rc, rd);
+      const float rs = (ra + rb) + (rc + rd);
       l = l * alpha + rs;
       tmem_wait_st();
       tc_fence_before();
