@@ -73,6 +73,15 @@ PU_API const char* pu_last_error(void);
 PU_API int pu_device_status(int* detail);
 
 /*
+ * Failure-detection self-test (no reference counterpart): launches one CTA
+ * that waits, with the same bounded mbarrier wait the attention kernels
+ * use, on a barrier nothing completes, giving up after `timeout_ns`
+ * (<= 2 s).  A following pu_device_status() returns PU_ERR_DEVICE_TIMEOUT
+ * with detail 901; the CUDA context remains usable.
+ */
+PU_API int pu_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
+/*
  * Training attention forward.
  * Replaces pallas_flash_attention (src/pallas_flash/ops/interface.py:20-85),
  * whose kernel is flash_attention_kernel (kernels/attention.py:11-36) running

@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include "pu_host.cuh"
+#include "pu_ptx.cuh"
 
 namespace pu {
 
@@ -139,3 +140,31 @@ int pu_device_status(int* detail) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Failure-detection self-test: one CTA waits on an mbarrier that nothing
+// completes, with the given bound, exactly as the attention kernels wait on
+// their pipelines.  The wait runs out, the kernel records
+// PU_ERR_DEVICE_TIMEOUT at kSiteSelfTest and returns; the context stays usable.
+// ---------------------------------------------------------------------------
+namespace pu {
+__global__ void selftest_timeout_kernel(uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);      // expects one arrival that never comes
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  mbar_wait(&bar, 0, &abort_flag, kSiteSelfTest, timeout_ns);
+}
+}  // namespace pu
+
+extern "C" int pu_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
+  if (timeout_ns == 0 || timeout_ns > pu::kWaitTimeoutNs)
+    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "self-test timeout must be in (0, %llu] ns",
+                         static_cast<unsigned long long>(pu::kWaitTimeoutNs));
+  pu::selftest_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(timeout_ns);
+  return pu::check_cuda(cudaGetLastError(), "self-test launch");
+}

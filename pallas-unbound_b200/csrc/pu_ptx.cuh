@@ -113,7 +113,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // status word and raising the CTA's abort flag) if it does not complete
 // within kWaitTimeoutNs, or immediately if the CTA is already aborting.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int where) {
+                                          int where, uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;   // common case: already complete
 #pragma unroll 1
@@ -125,7 +125,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if (global_timer_ns() - t0 > timeout_ns) {
       *abort_flag = 1;
       record_device_error(PU_ERR_DEVICE_TIMEOUT, where);
       return false;

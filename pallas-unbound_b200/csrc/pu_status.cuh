@@ -37,6 +37,7 @@ enum WaitSite : int {
   kSiteBwdDq = 206,
   kSiteBwdKV = 207,
   kSiteDecodeCounter = 301,
+  kSiteSelfTest = 901,
 };
 
 // Defined once: the library is a single translation unit.

@@ -35,6 +35,7 @@ SIGNATURES = {
     "pu_version": (ctypes.c_char_p, []),
     "pu_last_error": (ctypes.c_char_p, []),
     "pu_device_status": (_int, [ctypes.POINTER(_int)]),
+    "pu_selftest_wait_timeout": (_int, [ctypes.c_uint64, _c_void_p]),
     "pu_attn_fwd": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                            _i64, _i64, _i64, _i64, _i64, _float, _int, _c_void_p]),
     "pu_attn_bwd_workspace_size": (_size_t, [_i64, _i64, _i64, _i64]),
