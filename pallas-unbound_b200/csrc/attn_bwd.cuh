@@ -390,17 +390,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ============================================================================
 template <int D>
 struct CfgQ {
-  static constexpr int NS = 2;                   // K / V ring depth
+  // K_j is read twice (S_j early, dQ_j last), so its ring is one deeper than
+  // V's: the load of K_{j+2} starts as soon as dQ_{j-1} has finished.
+  static constexpr int NSK = 3;                  // K ring depth
+  static constexpr int NSV = 2;                  // V ring depth
   static constexpr int kTileQ = BM * D * 2;
   static constexpr int kTileKV = BN * D * 2;
   static constexpr int kColBlocks = D / 64;
   static constexpr int kOffQ = 0;
   static constexpr int kOffDO = kOffQ + kTileQ;
   static constexpr int kOffK = kOffDO + kTileQ;
-  static constexpr int kOffV = kOffK + NS * kTileKV;
-  static constexpr int kOffBar = kOffV + NS * kTileKV;
-  // barriers: QdO, Kf[NS], Ke[NS], Vf[NS], Ve[NS], S, dP, Sread, dPread, dS, dQdone
-  static constexpr int kNumBars = 1 + 4 * NS + 6;
+  static constexpr int kOffV = kOffK + NSK * kTileKV;
+  static constexpr int kOffBar = kOffV + NSV * kTileKV;
+  // barriers: QdO, Kf[NSK], Ke[NSK], Vf[NSV], Ve[NSV], S, dP, Sread, dPread, dS, dQdone
+  static constexpr int kNumBars = 1 + 2 * NSK + 2 * NSV + 6;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256, kColDS = 384;
@@ -427,10 +430,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* bQ = bars;
   uint64_t* bKf = bars + 1;
-  uint64_t* bKe = bKf + C::NS;
-  uint64_t* bVf = bKe + C::NS;
-  uint64_t* bVe = bVf + C::NS;
-  uint64_t* bS = bVe + C::NS;
+  uint64_t* bKe = bKf + C::NSK;
+  uint64_t* bVf = bKe + C::NSK;
+  uint64_t* bVe = bVf + C::NSV;
+  uint64_t* bS = bVe + C::NSV;
   uint64_t* bDP = bS + 1;
   uint64_t* bSr = bDP + 1;      // S_j read by the compute warps
   uint64_t* bDPr = bSr + 1;     // dP_j read
@@ -448,9 +451,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(bQ, 1);
-    for (int s = 0; s < C::NS; ++s) {
+    for (int s = 0; s < C::NSK; ++s) {
       mbar_init(bKf + s, 1);
       mbar_init(bKe + s, 1);
+    }
+    for (int s = 0; s < C::NSV; ++s) {
       mbar_init(bVf + s, 1);
       mbar_init(bVe + s, 1);
     }
@@ -485,16 +490,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(sDO + cb * BM * 128, &tmDO, bQ, cb * 64, q0, bh);
       }
       for (int j = 0; j < n_blocks; ++j) {
-        const int st = j % C::NS;
-        const uint32_t u = j / C::NS;
-        if (u > 0 && !mbar_wait(bKe + st, (u - 1) & 1, abort_flag, kSiteBwdEmpty)) break;
-        mbar_arrive_expect_tx(bKf + st, C::kTileKV);
+        const int sk = j % C::NSK, sv = j % C::NSV;
+        const uint32_t uk = j / C::NSK, uv = j / C::NSV;
+        if (uk > 0 && !mbar_wait(bKe + sk, (uk - 1) & 1, abort_flag, kSiteBwdEmpty)) break;
+        mbar_arrive_expect_tx(bKf + sk, C::kTileKV);
         for (int cb = 0; cb < C::kColBlocks; ++cb)
-          tma_load_3d(sK + st * C::kTileKV + cb * BN * 128, &tmK, bKf + st, cb * 64, j * BN, bh);
-        if (u > 0 && !mbar_wait(bVe + st, (u - 1) & 1, abort_flag, kSiteBwdEmpty)) break;
-        mbar_arrive_expect_tx(bVf + st, C::kTileKV);
+          tma_load_3d(sK + sk * C::kTileKV + cb * BN * 128, &tmK, bKf + sk, cb * 64, j * BN, bh);
+        if (uv > 0 && !mbar_wait(bVe + sv, (uv - 1) & 1, abort_flag, kSiteBwdEmpty)) break;
+        mbar_arrive_expect_tx(bVf + sv, C::kTileKV);
         for (int cb = 0; cb < C::kColBlocks; ++cb)
-          tma_load_3d(sV + st * C::kTileKV + cb * BN * 128, &tmV, bVf + st, cb * 64, j * BN, bh);
+          tma_load_3d(sV + sv * C::kTileKV + cb * BN * 128, &tmV, bVf + sv, cb * 64, j * BN, bh);
       }
     }
   } else if (warp == 9) {
@@ -525,38 +530,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(bDP);
       }
       for (int j = 0; ok && j < n_blocks; ++j) {
-        const int st = j % C::NS;
-        const int nst = (j + 1) % C::NS;
-        const uint32_t un = (j + 1) / C::NS;
+        const int sk = j % C::NSK, sv = j % C::NSV;
+        const int nsk = (j + 1) % C::NSK, nsv = (j + 1) % C::NSV;
+        const uint32_t unk = (j + 1) / C::NSK, unv = (j + 1) / C::NSV;
         const bool more = j + 1 < n_blocks;
         // S_{j+1} once S_j has been read
         if (!mbar_wait(bSr, j & 1, abort_flag, kSiteBwdSoftmax)) break;
         if (more) {
-          if (!mbar_wait(bKf + nst, un & 1, abort_flag, kSiteBwdLoad)) break;
+          if (!mbar_wait(bKf + nsk, unk & 1, abort_flag, kSiteBwdLoad)) break;
           tc_fence_after();
-          issue_ss(C::kColS, aQ, smem_u32(sK + nst * C::kTileKV));
+          issue_ss(C::kColS, aQ, smem_u32(sK + nsk * C::kTileKV));
           mma_commit(bS);
         }
         // dP_{j+1} once dP_j has been read
         if (!mbar_wait(bDPr, j & 1, abort_flag, kSiteBwdSoftmax)) break;
-        mma_commit(bVe + st);                // V_j's only reader (dP_j) has completed
+        mma_commit(bVe + sv);                // V_j's only reader (dP_j) has completed
         if (more) {
-          if (!mbar_wait(bVf + nst, un & 1, abort_flag, kSiteBwdLoad)) break;
+          if (!mbar_wait(bVf + nsv, unv & 1, abort_flag, kSiteBwdLoad)) break;
           tc_fence_after();
-          issue_ss(C::kColDP, aDO, smem_u32(sV + nst * C::kTileKV));
+          issue_ss(C::kColDP, aDO, smem_u32(sV + nsv * C::kTileKV));
           mma_commit(bDP);
         }
         // dQ += dS_j K_j
         if (!mbar_wait(bDS, j & 1, abort_flag, kSiteBwdDs)) break;
         tc_fence_after();
-        const uint64_t dk = make_sdesc_sw128(smem_u32(sK + st * C::kTileKV), BN * 128, 1024);
+        const uint64_t dk = make_sdesc_sw128(smem_u32(sK + sk * C::kTileKV), BN * 128, 1024);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           mma_ts(tmem + C::kColDQ, tmem + C::kColDS + kk * 8, sdesc_add(dk, kk * 16 * 128), idQ,
                  (j > 0 || kk > 0));
         }
         mma_commit(bDQd);
-        mma_commit(bKe + st);
+        mma_commit(bKe + sk);
       }
     }
   } else {
