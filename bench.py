@@ -346,6 +346,79 @@ def bench_decode(steps: int, warmup: int, rank: int, world: int):
     return us, kus, 2 * DEC_B * DEC_H * n_local * DEC_D * 2
 
 
+RAG_B, RAG_H, RAG_NCAP, RAG_D, RAG_PAGE = 8, 16, 131072, 128, 64
+
+
+def ragged_lens():
+    """Per-sequence lengths U[4096, 131072] rounded up to 128 (seeded)."""
+    import numpy as np
+    rng = np.random.Generator(np.random.PCG64(4))
+    return (np.ceil(rng.uniform(4096, RAG_NCAP, size=RAG_B) / 128) * 128).astype(np.int32)
+
+
+def _timed(fn, steps, flush, stream):
+    import torch
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.median(times) * 1e3
+
+
+def bench_ragged_decode(steps: int, warmup: int, rank: int, world: int):
+    """Batched ragged decode (B=8, H=16, D=128, fp16, lengths U[4096, 131072]):
+    the dense padded cache sequence-sharded over the ranks, and (one GPU) the
+    same tokens in a paged cache of 64-token pages in shuffled order.
+    Returns (dense us, paged us or None, algorithmic bytes of all ranks)."""
+    import numpy as np
+    import torch
+    from pallas_flash.kernels import decoding as dec
+    from pallas_flash.kernels import paged
+
+    lens = ragged_lens()
+    n_local = RAG_NCAP // world
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4000 + rank)
+    q = torch.randn((RAG_B, RAG_H, 1, RAG_D), device="cuda", generator=g).to(torch.float16)
+    k = torch.randn((RAG_B, RAG_H, n_local, RAG_D), device="cuda", generator=g).to(torch.float16)
+    v = torch.randn((RAG_B, RAG_H, n_local, RAG_D), device="cuda", generator=g).to(torch.float16)
+    lens_t = torch.from_numpy(lens).cuda()
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        group = dist.group.WORLD
+
+    def dense():
+        return dec.pallas_flash_decoding(q, k, v, kv_lens=lens_t, group=group)
+
+    for _ in range(warmup):
+        dense()
+    torch.cuda.synchronize()
+    barrier(world)
+    dense_us = allreduce_max(_timed(dense, steps, flush, stream), world)
+    paged_us = None
+    if world == 1:
+        cache = paged.PagedKVCache.from_dense(k, v, lens, page_size=RAG_PAGE, shuffle_seed=1)
+        del k, v
+
+        def run_paged():
+            return cache.decode(q)
+
+        for _ in range(warmup):
+            run_paged()
+        torch.cuda.synchronize()
+        paged_us = _timed(run_paged, steps, flush, stream)
+    nbytes = int(lens.astype(np.int64).sum()) * RAG_H * RAG_D * 2 * 2
+    return dense_us, paged_us, nbytes
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -371,6 +444,8 @@ def main():
     fwd_ms_max = allreduce_max(fwd_ms, world)
     e2e_dt, h2d, d2h = bench_attention_e2e(max(1, args.e2e_steps), 1, rank, world)
     dec_us, dec_kus, dec_bytes = bench_decode(max(5, min(args.steps, 50)), warmup, rank, world)
+    rag_us, rag_paged_us, rag_bytes = bench_ragged_decode(max(5, min(args.steps, 20)), warmup,
+                                                          rank, world)
 
     if rank == 0:
         bwd_flops = FWD_FLOPS * 2.5
@@ -429,6 +504,22 @@ def main():
                                     "traffic": NCU_TRAFFIC_BYTES["split_kv"] if world == 1 else None},
                        "l2": "256 MB buffer written before every step"},
         }
+        hbm = peaks["hbm_gbs"]
+        line["decode_ragged"] = {
+            "workload": f"ragged split-KV decode B={RAG_B} H={RAG_H} D={RAG_D} fp16, lengths "
+                        f"U[4096,{RAG_NCAP}] rounded to 128 (seeded), dense cache padded to "
+                        f"{RAG_NCAP} and sequence-sharded over {world} GPU(s)",
+            "algorithmic_bytes": rag_bytes,
+            "dense": {"us_per_step": round(rag_us, 2),
+                      "GB_s": round(rag_bytes / (rag_us * 1e-6) / 1e9, 1),
+                      "frac": round(rag_bytes / (rag_us * 1e-6) / 1e9 / (hbm * world), 4)},
+            "l2": "256 MB buffer written before every step"}
+        if rag_paged_us is not None:
+            line["decode_ragged"]["paged"] = {
+                "page_size": RAG_PAGE, "page_order": "shuffled",
+                "us_per_step": round(rag_paged_us, 2),
+                "GB_s": round(rag_bytes / (rag_paged_us * 1e-6) / 1e9, 1),
+                "frac": round(rag_bytes / (rag_paged_us * 1e-6) / 1e9 / hbm, 4)}
         if world == 1:
             dus, dsample = cpu_decode_sample()
             line["decode"]["cpu_baseline"] = {"value": round(dus, 1), "unit": "us/step",

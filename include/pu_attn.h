@@ -203,6 +203,58 @@ PU_API int pu_decode_noalloc(const void* q, int q_dtype,
                              int64_t B, int64_t H, int64_t n, int64_t D,
                              float sm_scale, void* stream);
 
+/*
+ * Paged KV cache.  No counterpart in the reference: its decode reads a
+ * dense, padded [B,H,N,D] cache (src/pallas_flash/kernels/decoding.py:86-103,
+ * 113-115) and has no cache-update op.  A paged cache lets sequences grow
+ * without copying the cache:
+ *   k_pool, v_pool: [num_pages][H][page_size][D], fp16 or bf16 (kv_dtype);
+ *     page p, head h holds page_size consecutive tokens of one sequence.
+ *   page_table: int32 [B][max_pages_per_seq]; entry i of sequence b is the
+ *     physical page of tokens [i*page_size, (i+1)*page_size).
+ *   kv_lens: int32 [B], tokens held by each sequence (required).
+ *   page_size: a power of two in [16, 4096].
+ * Only the first ceil(kv_lens[b] / page_size) table entries of a sequence
+ * are read.  An entry outside [0, num_pages) is not followed: the kernel
+ * records PU_ERR_INVALID_ARGUMENT in the device status word
+ * (pu_device_status, detail 302 for decode, 303 for append) and skips those
+ * tokens.
+ */
+
+/* Bytes of workspace pu_decode_paged needs (0 on invalid sizes). */
+PU_API size_t pu_decode_paged_workspace_size(int64_t B, int64_t H, int64_t max_pages_per_seq,
+                                             int64_t page_size, int64_t D);
+
+/*
+ * Decode step over a paged cache: same results as pu_decode on the dense
+ * cache the pages describe.  q [B,H,1,D] f16/bf16; o bf16 [B,H,1,D];
+ * lse fp32 [B,H] or NULL; workspace zeroed before its first use (the
+ * kernel leaves it zeroed).
+ */
+PU_API int pu_decode_paged(const void* q, int q_dtype,
+                           const void* k_pool, const void* v_pool, int kv_dtype,
+                           const int32_t* page_table, int64_t max_pages_per_seq,
+                           int64_t num_pages, int64_t page_size,
+                           const int32_t* kv_lens, void* o, float* lse,
+                           void* workspace, size_t workspace_bytes,
+                           int64_t B, int64_t H, int64_t D,
+                           float sm_scale, void* stream);
+
+/*
+ * Append one token per sequence to a paged cache: writes k_new/v_new
+ * [B,H,1,D] (kv_dtype) at position kv_lens[b] (page
+ * page_table[b][kv_lens[b] / page_size]) of every head, then advances
+ * kv_lens[b] by one, all on `stream`.  The caller maps a page into the
+ * table before a sequence crosses into it; a position past the table
+ * (kv_lens[b] >= max_pages_per_seq * page_size) or an invalid entry is
+ * reported as above and leaves that sequence unchanged.
+ */
+PU_API int pu_kv_append(const void* k_new, const void* v_new, int kv_dtype,
+                        void* k_pool, void* v_pool,
+                        const int32_t* page_table, int64_t max_pages_per_seq,
+                        int64_t num_pages, int64_t page_size, int32_t* kv_lens,
+                        int64_t B, int64_t H, int64_t D, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

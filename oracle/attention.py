@@ -30,6 +30,12 @@ leg.  It restates, in numpy, the arithmetic of the reference project
                            of pipeline.py:47-52 applied across shards, which
                            is what the reference documents for split-KV
                            decode (README.md:41-46) but never implements.
+  * `paged_to_dense` / `paged_append` — the paged KV cache (page pool +
+                           page table) the paged decode and append kernels
+                           use; no reference counterpart (the reference's
+                           decode reads a dense cache, decoding.py:86-103),
+                           so these define the layout the kernels are
+                           checked against.
 
 Parity pinning: the reference cannot run in this environment (it needs JAX
 and a TPU; JAX is not installed), so no reference outputs exist to compare
@@ -279,6 +285,53 @@ def decode_partial(q, k_shard, v_shard, *, kv_offset: int, kv_lens=None,
             r[1] = p.sum()
             r[2:] = p @ vh
     return out
+
+
+def paged_to_dense(pool, page_table, kv_lens, page_size: int, n: int | None = None):
+    """Gather a paged cache pool [P, H, page_size, D] into a dense [B, H, n, D] cache.
+
+    Token t of sequence b is row t % page_size of page page_table[b, t // page_size];
+    positions at or past kv_lens[b] are left zero.  The reference has no
+    paged cache (its decode reads a dense [B,H,N,D] cache, decoding.py:86-103):
+    this is the definition the paged kernels are checked against.
+    """
+    pool = np.asarray(pool)
+    table = np.asarray(page_table)
+    B = table.shape[0]
+    _, H, ps, D = pool.shape
+    assert ps == page_size
+    if n is None:
+        n = table.shape[1] * page_size
+    out = np.zeros((B, H, n, D), dtype=pool.dtype)
+    for b in range(B):
+        L = int(kv_lens[b])
+        for t0 in range(0, L, page_size):
+            rows = min(page_size, L - t0)
+            out[b, :, t0:t0 + rows] = pool[table[b, t0 // page_size], :, :rows]
+    return out
+
+
+def paged_append(k_pool, v_pool, page_table, kv_lens, k_new, v_new, page_size: int):
+    """In-place append of one token per sequence; returns the new lengths.
+
+    Sequences whose next position has no valid page (past the table, or an
+    entry outside [0, P)) are left unchanged, as the append kernel does.
+    """
+    table = np.asarray(page_table)
+    lens = np.array(kv_lens, dtype=np.int64)
+    P = k_pool.shape[0]
+    for b in range(table.shape[0]):
+        pos = int(lens[b])
+        slot = pos // page_size
+        if pos < 0 or slot >= table.shape[1]:
+            continue
+        pg = int(table[b, slot])
+        if not 0 <= pg < P:
+            continue
+        k_pool[pg, :, pos % page_size] = k_new[b, :, 0]
+        v_pool[pg, :, pos % page_size] = v_new[b, :, 0]
+        lens[b] = pos + 1
+    return lens
 
 
 def lse_combine(partials):

@@ -51,6 +51,12 @@ struct Params {
   __nv_bfloat16* o;      // final mode: [BH][D]
   float* lse;            // final mode: [BH] or nullptr
   float* partial;        // partial mode: [BH][D+2] (natural-log m)
+  // paged cache: k / v are page pools [num_pages][H][page_size][D]; token t of
+  // sequence b lives in page page_table[b * max_pages + t / page_size]
+  const int32_t* page_table;
+  int max_pages;
+  int num_pages;
+  int page_shift;        // log2(page_size)
 };
 
 template <typename T>
@@ -107,7 +113,7 @@ __device__ __forceinline__ void merge_records(const float* rec, int nrec, int st
   }
 }
 
-template <typename QT, typename KVT, int D, bool kFinal>
+template <typename QT, typename KVT, int D, bool kFinal, bool kPaged>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Params p) {
   constexpr int LPR = D / 8;        // lanes per cache row
   constexpr int RPW = 32 / LPR;     // rows per warp instruction
@@ -148,6 +154,27 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
 
   const KVT* kb = static_cast<const KVT*>(p.k) + (size_t)bh * p.n_local * D + sub * 8;
   const KVT* vb = static_cast<const KVT*>(p.v) + (size_t)bh * p.n_local * D + sub * 8;
+  // element offset of token t's row (dense: contiguous; paged: via the page
+  // table, with out-of-range page numbers reported and the token skipped)
+  const int h = bh % p.H;
+  auto row_off = [&](int t, bool& valid) -> size_t {
+    if constexpr (kPaged) {
+      const int pg = __ldg(p.page_table + (size_t)b * p.max_pages + (t >> p.page_shift));
+      valid = (unsigned)pg < (unsigned)p.num_pages;
+      if (!valid) {
+        record_device_error(PU_ERR_INVALID_ARGUMENT, kSiteDecodePage);
+        return 0;
+      }
+      return ((((size_t)pg * p.H + h) << p.page_shift) + (t & ((1 << p.page_shift) - 1))) * D + sub * 8;
+    } else {
+      valid = true;
+      return (size_t)t * D;
+    }
+  };
+  if constexpr (kPaged) {
+    kb = static_cast<const KVT*>(p.k);
+    vb = static_cast<const KVT*>(p.v);
+  }
 
   float m = -INFINITY, l = 0.f;
   float o[8];
@@ -156,13 +183,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
 
   for (int base = t_begin + warp * RPW * kUnroll; base < t_end; base += ROWS_PER_ITER) {
     uint4 kw[kUnroll], vw[kUnroll];
+    bool tok_ok[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int t = base + u * RPW + rw;
+      tok_ok[u] = false;
       if (t < t_end) {
-        kw[u] = ld_stream(reinterpret_cast<const uint4*>(kb + (size_t)t * D));
-        vw[u] = ld_stream(reinterpret_cast<const uint4*>(vb + (size_t)t * D));
-      } else {
+        const size_t off = row_off(t, tok_ok[u]);
+        if (tok_ok[u]) {
+          kw[u] = ld_stream(reinterpret_cast<const uint4*>(kb + off));
+          vw[u] = ld_stream(reinterpret_cast<const uint4*>(vb + off));
+        }
+      }
+      if (!tok_ok[u]) {
         kw[u] = make_uint4(0, 0, 0, 0);
         vw[u] = make_uint4(0, 0, 0, 0);
       }
@@ -185,8 +218,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
     float gmax = -INFINITY;
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const int t = base + u * RPW + rw;
-      if (t >= t_end) s[u] = -INFINITY;
+      if (!tok_ok[u]) s[u] = -INFINITY;
       gmax = fmaxf(gmax, s[u]);
     }
     const float m_new = fmaxf(m, gmax);
@@ -308,14 +340,14 @@ struct Plan {
 
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms) {
+inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms, long long align = 16) {
   Plan pl{};
   const long long target = (long long)num_sms * kCtasPerSm * kWaves;
   long long splits = (target + BH - 1) / BH;
   const long long max_splits = std::max<long long>(1, (n_local + kMinChunk - 1) / kMinChunk);
   splits = std::max<long long>(1, std::min(splits, max_splits));
   long long chunk = (n_local + splits - 1) / splits;
-  chunk = std::max<long long>(16, (chunk + 15) / 16 * 16);
+  chunk = std::max<long long>(align, (chunk + align - 1) / align * align);
   splits = std::max<long long>(1, (n_local + chunk - 1) / chunk);
   pl.splits = (int)splits;
   pl.chunk = (int)chunk;
@@ -324,11 +356,11 @@ inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms)
   return pl;
 }
 
-template <bool kFinal>
+template <bool kFinal, bool kPaged = false>
 int launch(const Params& prm, int q_dtype, int kv_dtype, int D, int BH, cudaStream_t st) {
   dim3 grid(prm.splits, BH);
   dim3 block(kThreads);
-#define PU_DECODE_LAUNCH(QT, KVT, DD) split_kv_kernel<QT, KVT, DD, kFinal><<<grid, block, 0, st>>>(prm)
+#define PU_DECODE_LAUNCH(QT, KVT, DD) split_kv_kernel<QT, KVT, DD, kFinal, kPaged><<<grid, block, 0, st>>>(prm)
   const bool qh = (q_dtype == PU_DTYPE_F16);
   const bool kh = (kv_dtype == PU_DTYPE_F16);
   if (D == 128) {

@@ -3,6 +3,7 @@
 // compiled together instead of with relocatable device code.
 #include "capi.cuh"
 #include "decode.cuh"
+#include "paged.cuh"
 #include "attn_fwd.cuh"
 #include "attn_bwd.cuh"
 

@@ -37,6 +37,8 @@ enum WaitSite : int {
   kSiteBwdDq = 206,
   kSiteBwdKV = 207,
   kSiteDecodeCounter = 301,
+  kSiteDecodePage = 302,
+  kSiteAppendPage = 303,
   kSiteSelfTest = 901,
 };
 

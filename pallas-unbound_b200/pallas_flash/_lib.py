@@ -54,6 +54,12 @@ SIGNATURES = {
     "pu_decode_noalloc": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p,
                                  _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _float,
                                  _c_void_p]),
+    "pu_decode_paged_workspace_size": (_size_t, [_i64, _i64, _i64, _i64, _i64]),
+    "pu_decode_paged": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _i64,
+                               _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _size_t,
+                               _i64, _i64, _i64, _float, _c_void_p]),
+    "pu_kv_append": (_int, [_c_void_p, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p, _i64,
+                            _i64, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p]),
 }
 
 _lock = threading.Lock()

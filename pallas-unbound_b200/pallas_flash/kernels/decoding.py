@@ -20,6 +20,9 @@ Keyword-only additions:
               partials are all-gathered over NCCL, and a fused stable-LSE
               kernel merges them (the split-KV scheme the reference documents,
               README.md:41-46, but never implements).
+  page_table  int32 [B, max_pages_per_seq]: the caches are then page pools
+              [num_pages, H, page_size, D] (see kernels/paged.py) and
+              kv_lens is required; single GPU only.
 """
 from __future__ import annotations
 
@@ -101,8 +104,14 @@ def decode_combine(parts: torch.Tensor, B: int, H: int, D: int, *, out=None, lse
 def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
                           kv_lens: Optional[torch.Tensor] = None,
                           sm_scale: Optional[float] = None, return_lse: bool = False,
-                          group=None):
+                          group=None, page_table: Optional[torch.Tensor] = None):
     """One decode step of attention for a query token per (b, h)."""
+    if page_table is not None:
+        from .paged import paged_decode
+        if group is not None or kv_lens is None:
+            raise ValueError("a paged cache needs kv_lens and runs on one GPU (group=None)")
+        return paged_decode(q, k_cache, v_cache, page_table, kv_lens, sm_scale=sm_scale,
+                            return_lse=return_lse)
     if q.dim() != 4 or q.shape[2] != 1:
         raise ValueError("q must be [B, H, 1, D]")
     if k_cache.shape != v_cache.shape or k_cache.shape[:2] != q.shape[:2] \
