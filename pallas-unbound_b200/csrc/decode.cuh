@@ -93,6 +93,17 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   return r;
 }
 
+// ld_stream when `pred`, else zeros; a predicated load, not a branch.
+__device__ __forceinline__ uint4 ld_stream_if(const uint4* p, bool pred) {
+  uint4 r = make_uint4(0, 0, 0, 0);
+  asm volatile(
+      "{\n .reg .pred q;\n setp.ne.b32 q, %5, 0;\n"
+      " @q ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];\n}"
+      : "+r"(r.x), "+r"(r.y), "+r"(r.z), "+r"(r.w)
+      : "l"(p), "r"((int)pred));
+  return r;
+}
+
 // Merge (m, l, o[D]) records with a stable LogSumExp; m in log2 units.
 // Thread `d` (< D) produces column d.  Returns M and L through refs.
 template <int D>
@@ -154,50 +165,73 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
 
   const KVT* kb = static_cast<const KVT*>(p.k) + (size_t)bh * p.n_local * D + sub * 8;
   const KVT* vb = static_cast<const KVT*>(p.v) + (size_t)bh * p.n_local * D + sub * 8;
-  // element offset of token t's row (dense: contiguous; paged: via the page
-  // table, with out-of-range page numbers reported and the token skipped)
+  // paged cache: token t of sequence b is row t % page_size of page
+  // page_table[b][t / page_size]; out-of-range page numbers are reported
+  // and their tokens skipped.  A warp's tokens of one iteration are TW
+  // consecutive tokens starting at a multiple of TW (chunks are multiples of
+  // the page size), so when page_size >= TW they share one page: its entry
+  // is read once, one iteration ahead of its use.
+  constexpr int TW = RPW * kUnroll;
   const int h = bh % p.H;
-  auto row_off = [&](int t, bool& valid) -> size_t {
-    if constexpr (kPaged) {
-      const int pg = __ldg(p.page_table + (size_t)b * p.max_pages + (t >> p.page_shift));
-      valid = (unsigned)pg < (unsigned)p.num_pages;
-      if (!valid) {
-        record_device_error(PU_ERR_INVALID_ARGUMENT, kSiteDecodePage);
-        return 0;
-      }
-      return ((((size_t)pg * p.H + h) << p.page_shift) + (t & ((1 << p.page_shift) - 1))) * D + sub * 8;
-    } else {
-      valid = true;
-      return (size_t)t * D;
-    }
-  };
+  const int32_t* table_b = nullptr;
+  bool one_page = false;
+  int pg_next = 0;
   if constexpr (kPaged) {
-    kb = static_cast<const KVT*>(p.k);
-    vb = static_cast<const KVT*>(p.v);
+    kb = static_cast<const KVT*>(p.k) + sub * 8;
+    vb = static_cast<const KVT*>(p.v) + sub * 8;
+    table_b = p.page_table + (size_t)b * p.max_pages;
+    one_page = (1 << p.page_shift) >= TW;
+    const int base0 = t_begin + warp * TW;
+    if (one_page && base0 < t_end) pg_next = __ldg(table_b + (base0 >> p.page_shift));
   }
+  const int page_mask = (1 << p.page_shift) - 1;
+  auto page_row = [&](int pg, int t) -> size_t {
+    return ((((size_t)pg * p.H + h) << p.page_shift) + (t & page_mask)) * D;
+  };
 
   float m = -INFINITY, l = 0.f;
   float o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i] = 0.f;
 
-  for (int base = t_begin + warp * RPW * kUnroll; base < t_end; base += ROWS_PER_ITER) {
+  for (int base = t_begin + warp * TW; base < t_end; base += ROWS_PER_ITER) {
     uint4 kw[kUnroll], vw[kUnroll];
     bool tok_ok[kUnroll];
+    if constexpr (kPaged) {
+      if (one_page) {
+        const int pg = pg_next;
+        // next iteration's entry (clamped to this chunk: always a valid index)
+        pg_next = __ldg(table_b + (min(base + ROWS_PER_ITER, t_end - 1) >> p.page_shift));
+        const bool page_ok = (unsigned)pg < (unsigned)p.num_pages;
+        if (!page_ok && lane == 0) record_device_error(PU_ERR_INVALID_ARGUMENT, kSiteDecodePage);
+        const size_t row0 = page_ok ? page_row(pg, base) : 0;
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int t = base + u * RPW + rw;
-      tok_ok[u] = false;
-      if (t < t_end) {
-        const size_t off = row_off(t, tok_ok[u]);
-        if (tok_ok[u]) {
-          kw[u] = ld_stream(reinterpret_cast<const uint4*>(kb + off));
-          vw[u] = ld_stream(reinterpret_cast<const uint4*>(vb + off));
+        for (int u = 0; u < kUnroll; ++u) {
+          tok_ok[u] = page_ok && (base + u * RPW + rw < t_end);
+          const size_t off = row0 + (size_t)(u * RPW + rw) * D;
+          kw[u] = ld_stream_if(reinterpret_cast<const uint4*>(kb + off), tok_ok[u]);
+          vw[u] = ld_stream_if(reinterpret_cast<const uint4*>(vb + off), tok_ok[u]);
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int t = base + u * RPW + rw;
+          int pg = -1;
+          if (t < t_end) pg = __ldg(table_b + (t >> p.page_shift));
+          tok_ok[u] = (unsigned)pg < (unsigned)p.num_pages;
+          if (t < t_end && !tok_ok[u]) record_device_error(PU_ERR_INVALID_ARGUMENT, kSiteDecodePage);
+          const size_t off = tok_ok[u] ? page_row(pg, t) : 0;
+          kw[u] = ld_stream_if(reinterpret_cast<const uint4*>(kb + off), tok_ok[u]);
+          vw[u] = ld_stream_if(reinterpret_cast<const uint4*>(vb + off), tok_ok[u]);
         }
       }
-      if (!tok_ok[u]) {
-        kw[u] = make_uint4(0, 0, 0, 0);
-        vw[u] = make_uint4(0, 0, 0, 0);
+    } else {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int t = base + u * RPW + rw;
+        tok_ok[u] = t < t_end;
+        kw[u] = ld_stream_if(reinterpret_cast<const uint4*>(kb + (size_t)t * D), tok_ok[u]);
+        vw[u] = ld_stream_if(reinterpret_cast<const uint4*>(vb + (size_t)t * D), tok_ok[u]);
       }
     }
     float s[kUnroll];
