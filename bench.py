@@ -293,7 +293,11 @@ def bench_attention_e2e(steps: int, warmup: int, rank: int, world: int):
     return dt, 4 * nbytes, 4 * nbytes
 
 
-def bench_decode(steps: int, warmup: int, rank: int, world: int):
+def bench_decode(steps: int, warmup: int, rank: int, world: int, transport: str = "peer"):
+    """Decode step time (median over steps, max over ranks), kernel-only time of
+    the local split-KV pass, and the K/V bytes one rank reads.  With more than
+    one rank the partials travel by `transport` ("peer": NVLink peer stores +
+    flags; "nccl": all-gather)."""
     import torch
     from pallas_flash.kernels import decoding as dec
 
@@ -311,7 +315,7 @@ def bench_decode(steps: int, warmup: int, rank: int, world: int):
     stream = torch.cuda.current_stream()
 
     def step():
-        return dec.pallas_flash_decoding(q, k, v, group=group)
+        return dec.pallas_flash_decoding(q, k, v, group=group, transport=transport)
 
     for _ in range(warmup):
         step()
@@ -320,6 +324,7 @@ def bench_decode(steps: int, warmup: int, rank: int, world: int):
     times = []
     kern = []
     for _ in range(steps):
+        barrier(world)                              # ranks start each step together
         flush.zero_()                               # evict the cache shard from L2
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -396,7 +401,7 @@ def bench_ragged_decode(steps: int, warmup: int, rank: int, world: int):
         group = dist.group.WORLD
 
     def dense():
-        return dec.pallas_flash_decoding(q, k, v, kv_lens=lens_t, group=group)
+        return dec.pallas_flash_decoding(q, k, v, kv_lens=lens_t, group=group, transport="peer")
 
     for _ in range(warmup):
         dense()
@@ -443,7 +448,9 @@ def main():
     bwd_ms_max = allreduce_max(bwd_ms, world)
     fwd_ms_max = allreduce_max(fwd_ms, world)
     e2e_dt, h2d, d2h = bench_attention_e2e(max(1, args.e2e_steps), 1, rank, world)
-    dec_us, dec_kus, dec_bytes = bench_decode(max(5, min(args.steps, 50)), warmup, rank, world)
+    dec_steps = max(5, min(args.steps, 50))
+    dec_us, dec_kus, dec_bytes = bench_decode(dec_steps, warmup, rank, world, "peer")
+    nccl_us = bench_decode(dec_steps, warmup, rank, world, "nccl")[0] if world > 1 else None
     rag_us, rag_paged_us, rag_bytes = bench_ragged_decode(max(5, min(args.steps, 20)), warmup,
                                                           rank, world)
 
@@ -494,10 +501,12 @@ def main():
             "gpu_launches": 4 * args.steps,
             "clocks": clk,
             "decode": {"workload": f"split-KV decode B=1 H=32 N=32768 D=128 fp16 cache, sequence-sharded over {world} GPU(s)"
-                                   + (", NCCL all-gather of (m,l,o) + fused combine" if world > 1 else ""),
+                                   + (", (m,l,o) records stored into every rank's exchange buffer over "
+                                      "NVLink + bounded-wait flag merge (no collective)" if world > 1 else ""),
                        "us_per_step": round(dec_us, 2),
                        "GB_s": round(dec_total_bytes / (dec_us * 1e-6) / 1e9, 1),
                        "kernel_us": round(dec_kus, 2),
+                       "nccl_allgather_us_per_step": round(nccl_us, 2) if nccl_us else None,
                        "roofline": {"bound": "hbm", "achieved": round(dec_bytes / (dec_kus * 1e-6) / 1e9, 1),
                                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                     "frac": round(dec_bytes / (dec_kus * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
@@ -527,6 +536,8 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        from pallas_flash.distributed import peer
+        peer.close_all()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -255,6 +255,52 @@ PU_API int pu_kv_append(const void* k_new, const void* v_new, int kv_dtype,
                         int64_t num_pages, int64_t page_size, int32_t* kv_lens,
                         int64_t B, int64_t H, int64_t D, void* stream);
 
+/*
+ * Sequence-sharded decode over NVLink peer memory (replaces the all-gather
+ * between pu_decode_partial and pu_decode_combine).  Replaces the same
+ * reference step as those two: the split-KV LogSumExp merge documented in
+ * README.md:41-46 for the mesh-sharded decode (kernels/decoding.py:105-145
+ * under distributed/mesh.py:57-77), which the reference never implements.
+ *
+ * Each of the G ranks (one process per GPU, G <= 8, GPUs with peer access)
+ * owns one exchange buffer of pu_decode_exchange_bytes(B,H,D,G) bytes,
+ * allocated zeroed by pu_peer_alloc, whose IPC handle it shares with the
+ * other ranks (any host channel); each rank opens the others' handles with
+ * pu_peer_open.  Per decode step, every rank calls, on its own stream and
+ * with the same epoch (1, 2, 3, ... in lockstep):
+ *   pu_decode_push: the split-KV pass over the local shard; the record of
+ *     each (b, h) is stored into every rank's exchange buffer and a flag is
+ *     raised there.  exchange[g] = this process's pointer to rank g's buffer
+ *     (its own allocation for g == rank).
+ *   pu_decode_pull: waits until all G ranks have published this epoch
+ *     (bounded by timeout_ns <= 2 s; on expiry pu_device_status reports
+ *     PU_ERR_DEVICE_TIMEOUT, detail 304, and o is zeros), then merges the
+ *     records exactly as pu_decode_combine: same o / lse on every rank.
+ * A rank must not free or close buffers while another rank may still push.
+ */
+#define PU_IPC_HANDLE_BYTES 64
+
+/* cudaMalloc + zero-fill a buffer and export its IPC handle (64 bytes). */
+PU_API int pu_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+PU_API int pu_peer_free(void* dev_ptr);
+/* Map another process's buffer (peer access enabled on first use). */
+PU_API int pu_peer_open(const void* ipc_handle, void** dev_ptr);
+PU_API int pu_peer_close(void* dev_ptr);
+
+PU_API size_t pu_decode_exchange_bytes(int64_t B, int64_t H, int64_t D, int64_t G);
+
+PU_API int pu_decode_push(const void* q, int q_dtype,
+                          const void* k_cache, const void* v_cache, int kv_dtype,
+                          const int32_t* kv_lens, int64_t kv_offset,
+                          void* const* exchange, int64_t G, int64_t rank, uint32_t epoch,
+                          void* workspace, size_t workspace_bytes,
+                          int64_t B, int64_t H, int64_t n_local, int64_t D,
+                          float sm_scale, void* stream);
+
+PU_API int pu_decode_pull(const void* exchange, int64_t G, uint32_t epoch,
+                          void* o, float* lse, int64_t B, int64_t H, int64_t D,
+                          uint64_t timeout_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,6 +33,7 @@ constexpr int kWaves = 4;         // CTAs per SM slot the split heuristic aims a
 constexpr int kMinChunk = 256;    // fewest tokens one CTA is given
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kMaxPeers = 8;      // ranks of a push-mode exchange (one NVLink domain)
 
 struct Params {
   const void* q;
@@ -57,6 +58,14 @@ struct Params {
   int max_pages;
   int num_pages;
   int page_shift;        // log2(page_size)
+  // push mode (sequence-sharded decode over peer memory): the shard's record
+  // for (b, h) goes to slot [epoch & 1][rank][bh] of every rank's exchange
+  // buffer as 64-bit words {value bits, epoch} (one store each, so a reader
+  // that sees the epoch sees the value: no fence, no separate flag)
+  unsigned long long* peer_rec[kMaxPeers];
+  int n_peers;
+  int rank;
+  unsigned epoch;
 };
 
 template <typename T>
@@ -124,7 +133,9 @@ __device__ __forceinline__ void merge_records(const float* rec, int nrec, int st
   }
 }
 
-template <typename QT, typename KVT, int D, bool kFinal, bool kPaged>
+// kFinal: write the bf16 output; else the shard partial (to `partial`, or to
+// every peer's exchange buffer when kPush).
+template <typename QT, typename KVT, int D, bool kFinal, bool kPaged, bool kPush = false>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Params p) {
   constexpr int LPR = D / 8;        // lanes per cache row
   constexpr int RPW = 32 / LPR;     // rows per warp instruction
@@ -323,6 +334,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
       if (tid == 0 && p.lse != nullptr) {
         p.lse[bh] = (L > 0.f) ? (M + lg2(L)) * kLn2 : -INFINITY;
       }
+    } else if constexpr (kPush) {
+      const float m_nat = (M == -INFINITY) ? -INFINITY : M * kLn2;
+      const size_t slot = ((size_t)((p.epoch & 1u) * p.n_peers + p.rank) * gridDim.y + bh) * (D + 2);
+#pragma unroll 1
+      for (int g = 0; g < p.n_peers; ++g) {
+        unsigned long long* out = p.peer_rec[g] + slot;
+        st_volatile_u64(out + 2 + tid, ll_word(O, p.epoch));
+        if (tid == 0) {
+          st_volatile_u64(out, ll_word(m_nat, p.epoch));
+          st_volatile_u64(out + 1, ll_word(L, p.epoch));
+        }
+      }
     } else {
       float* out = p.partial + (size_t)bh * (D + 2);
       out[2 + tid] = O;
@@ -333,6 +356,68 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
     }
   }
   if (tid == 0) p.ws_count[bh] = 0;  // leave the workspace zeroed for the next call
+}
+
+// Push-mode merge: wait (bounded) until the words of every rank's record for
+// this (b, h) carry `epoch`, then merge in rank order (the arithmetic of
+// combine_kernel).  A wait that runs out records PU_ERR_DEVICE_TIMEOUT
+// (detail kSiteDecodePeer) and the output is zeros.
+__device__ __forceinline__ bool ll_wait(const unsigned long long* w, unsigned epoch, uint64_t timeout_ns,
+                                        float& value) {
+  unsigned long long x = ld_volatile_u64(w);
+  if ((unsigned)(x >> 32) != epoch) {
+    const uint64_t t0 = global_timer_ns();
+    do {
+      if (global_timer_ns() - t0 > timeout_ns) return false;
+      x = ld_volatile_u64(w);
+    } while ((unsigned)(x >> 32) != epoch);
+  }
+  value = __uint_as_float((unsigned)x);
+  return true;
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) peer_combine_kernel(const unsigned long long* __restrict__ exch, int G,
+                                                         int BH, unsigned epoch, uint64_t timeout_ns,
+                                                         __nv_bfloat16* __restrict__ o,
+                                                         float* __restrict__ lse) {
+  const int bh = blockIdx.x;
+  const int d = threadIdx.x;
+  const unsigned long long* base = exch + (size_t)(epoch & 1u) * G * BH * (D + 2);
+  float mg[kMaxPeers], lg[kMaxPeers], og[kMaxPeers];
+  bool ok = true;
+#pragma unroll
+  for (int g = 0; g < kMaxPeers; ++g) {
+    mg[g] = -INFINITY;
+    lg[g] = 0.f;
+    og[g] = 0.f;
+    if (g < G && ok) {
+      const unsigned long long* r = base + ((size_t)g * BH + bh) * (D + 2);
+      ok = ll_wait(r, epoch, timeout_ns, mg[g]) && ll_wait(r + 1, epoch, timeout_ns, lg[g]) &&
+           ll_wait(r + 2 + d, epoch, timeout_ns, og[g]);
+    }
+  }
+  if (!__syncthreads_and(ok)) {
+    if (d == 0) record_device_error(PU_ERR_DEVICE_TIMEOUT, kSiteDecodePeer);
+    o[(size_t)bh * D + d] = __float2bfloat16_rn(0.f);
+    if (d == 0 && lse != nullptr) lse[bh] = -INFINITY;
+    return;
+  }
+  float M = -INFINITY;
+#pragma unroll
+  for (int g = 0; g < kMaxPeers; ++g) M = fmaxf(M, mg[g]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+#pragma unroll
+    for (int g = 0; g < kMaxPeers; ++g) {
+      if (g >= G || mg[g] == -INFINITY) continue;
+      const float w = ex2((mg[g] - M) * kLog2e);
+      L += w * lg[g];
+      O += w * og[g];
+    }
+  }
+  o[(size_t)bh * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+  if (d == 0 && lse != nullptr) lse[bh] = (L > 0.f) ? M + logf(L) : -INFINITY;
 }
 
 // Merge G gathered shard records {m (natural log), l, o[D]} per (b, h).
@@ -390,11 +475,11 @@ inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms,
   return pl;
 }
 
-template <bool kFinal, bool kPaged = false>
+template <bool kFinal, bool kPaged = false, bool kPush = false>
 int launch(const Params& prm, int q_dtype, int kv_dtype, int D, int BH, cudaStream_t st) {
   dim3 grid(prm.splits, BH);
   dim3 block(kThreads);
-#define PU_DECODE_LAUNCH(QT, KVT, DD) split_kv_kernel<QT, KVT, DD, kFinal, kPaged><<<grid, block, 0, st>>>(prm)
+#define PU_DECODE_LAUNCH(QT, KVT, DD) split_kv_kernel<QT, KVT, DD, kFinal, kPaged, kPush><<<grid, block, 0, st>>>(prm)
   const bool qh = (q_dtype == PU_DTYPE_F16);
   const bool kh = (kv_dtype == PU_DTYPE_F16);
   if (D == 128) {

@@ -4,6 +4,7 @@
 #include "capi.cuh"
 #include "decode.cuh"
 #include "paged.cuh"
+#include "peer.cuh"
 #include "attn_fwd.cuh"
 #include "attn_bwd.cuh"
 

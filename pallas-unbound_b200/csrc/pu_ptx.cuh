@@ -25,6 +25,22 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// 64-bit words {float bits, epoch} that other GPUs store over NVLink: one
+// naturally aligned 64-bit access each, so value and epoch arrive together.
+__device__ __forceinline__ unsigned long long ll_word(float v, unsigned epoch) {
+  return ((unsigned long long)epoch << 32) | __float_as_uint(v);
+}
+
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ bool elect_one_sync() {
   uint32_t pred = 0;
   asm volatile(

@@ -39,6 +39,7 @@ enum WaitSite : int {
   kSiteDecodeCounter = 301,
   kSiteDecodePage = 302,
   kSiteAppendPage = 303,
+  kSiteDecodePeer = 304,
   kSiteSelfTest = 901,
 };
 

@@ -58,6 +58,16 @@ SIGNATURES = {
     "pu_decode_paged": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _i64,
                                _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _size_t,
                                _i64, _i64, _i64, _float, _c_void_p]),
+    "pu_peer_alloc": (_int, [_size_t, ctypes.POINTER(_c_void_p), _c_void_p]),
+    "pu_peer_free": (_int, [_c_void_p]),
+    "pu_peer_open": (_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "pu_peer_close": (_int, [_c_void_p]),
+    "pu_decode_exchange_bytes": (_size_t, [_i64, _i64, _i64, _i64]),
+    "pu_decode_push": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _i64,
+                              _c_void_p, _i64, _i64, ctypes.c_uint32, _c_void_p, _size_t,
+                              _i64, _i64, _i64, _i64, _float, _c_void_p]),
+    "pu_decode_pull": (_int, [_c_void_p, _i64, ctypes.c_uint32, _c_void_p, _c_void_p, _i64,
+                              _i64, _i64, ctypes.c_uint64, _c_void_p]),
     "pu_kv_append": (_int, [_c_void_p, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p, _i64,
                             _i64, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p]),
 }

@@ -20,6 +20,10 @@ Keyword-only additions:
               partials are all-gathered over NCCL, and a fused stable-LSE
               kernel merges them (the split-KV scheme the reference documents,
               README.md:41-46, but never implements).
+  transport   for a sharded cache: "nccl" (all-gather of the partials) or
+              "peer" (partials stored straight into every rank's exchange
+              buffer over NVLink, flags instead of a collective; see
+              distributed/peer.py)
   page_table  int32 [B, max_pages_per_seq]: the caches are then page pools
               [num_pages, H, page_size, D] (see kernels/paged.py) and
               kv_lens is required; single GPU only.
@@ -104,7 +108,8 @@ def decode_combine(parts: torch.Tensor, B: int, H: int, D: int, *, out=None, lse
 def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
                           kv_lens: Optional[torch.Tensor] = None,
                           sm_scale: Optional[float] = None, return_lse: bool = False,
-                          group=None, page_table: Optional[torch.Tensor] = None):
+                          group=None, transport: str = "nccl",
+                          page_table: Optional[torch.Tensor] = None):
     """One decode step of attention for a query token per (b, h)."""
     if page_table is not None:
         from .paged import paged_decode
@@ -143,14 +148,23 @@ def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch
                                  o.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), B, H,
                                  n_local, D, float(sm_scale), stream), "pu_decode")
     else:
-        from ..distributed.collectives import all_gather_partials
         import torch.distributed as dist
         rank = dist.get_rank(group)
         world = dist.get_world_size(group)
-        part = decode_partial(q_, k_, v_, kv_offset=rank * n_local, kv_lens=lens,
-                              sm_scale=sm_scale)
-        gathered = all_gather_partials(part, world, group)
-        o, lse = decode_combine(gathered, B, H, D)
+        if transport == "peer":
+            from ..distributed.peer import get_exchange
+            ex = get_exchange(B, H, D, group)
+            ws = DecodeWorkspace.get(dev, int(lib.pu_decode_workspace_size(B, H, n_local, D)))
+            o, lse = ex.decode(q_, k_, v_, kv_offset=rank * n_local, kv_lens=lens,
+                               sm_scale=sm_scale, workspace=ws)
+        elif transport == "nccl":
+            from ..distributed.collectives import all_gather_partials
+            part = decode_partial(q_, k_, v_, kv_offset=rank * n_local, kv_lens=lens,
+                                  sm_scale=sm_scale)
+            gathered = all_gather_partials(part, world, group)
+            o, lse = decode_combine(gathered, B, H, D)
+        else:
+            raise ValueError(f"unknown transport {transport!r} (nccl or peer)")
     if host:
         o, lse = o.cpu(), lse.cpu()
     return (o, lse) if return_lse else o

@@ -4,6 +4,11 @@
   the KV cache, runs pu_decode_partial, the packed (m, l, o) partials move
   with one NCCL all-gather, and pu_decode_combine merges them; every rank
   must match the oracle's whole-cache decode.
+* The same decode over NVLink peer memory (pu_decode_push / pu_decode_pull,
+  no collective): bit-identical to the NCCL path over consecutive steps
+  (both exchange slots), and a merge whose peers never publish runs out of
+  its bounded wait, is reported (PU_ERR_DEVICE_TIMEOUT, detail 304), and
+  leaves the context usable.
 * Head-partitioned training attention: each rank runs forward + backward
   on its heads only (no collective); the gathered outputs match the oracle.
 Runs world_size 2 as spawned processes with NCCL_NVLS_ENABLE=0.
@@ -62,6 +67,30 @@ def _worker(rank, world, port, out_dir):
     ro, rl = orc.decode_forward(q.float().numpy(), k.float().numpy(), v.float().numpy(), kv_lens=lens.numpy())
     res["dec_o"] = orc.compare(o.float().cpu().numpy(), ro)
     res["dec_lse"] = orc.compare(lse.cpu().numpy(), rl)
+    # --- the same decode over peer memory, several steps ---
+    from pallas_flash import _lib
+    from pallas_flash.distributed import peer
+    same = True
+    for step in range(5):
+        qs = randn((B, H, 1, D), 90 + step, dtype=torch.float16).cuda()
+        o_n, l_n = pallas_flash_decoding(qs, ks, vs, kv_lens=lens.cuda(), group=dist.group.WORLD,
+                                         return_lse=True)
+        o_p, l_p = pallas_flash_decoding(qs, ks, vs, kv_lens=lens.cuda(), group=dist.group.WORLD,
+                                         transport="peer", return_lse=True)
+        same &= bool(torch.equal(o_n, o_p)) and bool(torch.equal(l_n, l_p))
+    res["peer_equal"] = same
+    res["peer_status"] = list(_lib.device_status())
+    ex = peer.get_exchange(B, H, D, dist.group.WORLD)
+    o_t = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device="cuda")
+    # an epoch no rank will publish: the wait must run out (50 ms) and report
+    _lib.check(_lib.lib().pu_decode_pull(ex._local, world, ex.epoch + 1000, o_t.data_ptr(), None,
+                                         B, H, D, 50_000_000, torch.cuda.current_stream().cuda_stream),
+               "pu_decode_pull")
+    res["timeout_status"] = list(_lib.device_status())
+    o_p, _ = pallas_flash_decoding(q.cuda(), ks, vs, kv_lens=lens.cuda(), group=dist.group.WORLD,
+                                   transport="peer", return_lse=True)
+    res["after_timeout"] = orc.compare(o_p.float().cpu().numpy(), ro)
+    peer.close_all()
     # --- head-partitioned training attention ---
     B, H, N, D = 1, 4, 512, 128
     qg, kg, vg, dog = (randn((B, H, N, D), 80 + i) for i in range(4))
@@ -94,6 +123,9 @@ def test_two_gpu_decode_and_partitioned_training(tmp_path, built_lib):
         res = json.loads(Path(tmp_path, f"rank{rank}.json").read_text())
         assert res["dec_o"]["max_abs"] <= 2e-2 and res["dec_o"]["rel"] <= 1e-2, res
         assert res["dec_lse"]["max_abs"] <= 1e-3, res
+        assert res["peer_equal"] and res["peer_status"] == [0, 0], res
+        assert res["timeout_status"] == [5, 304], res
+        assert res["after_timeout"]["max_abs"] <= 2e-2 and res["after_timeout"]["rel"] <= 1e-2, res
         assert res["tr_o"]["max_abs"] <= 2e-2 and res["tr_o"]["rel"] <= 1e-2, res
         for g in ("dq", "dk", "dv"):
             assert res["tr_" + g]["rel"] <= 3e-2, res
