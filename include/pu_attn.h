@@ -13,7 +13,8 @@
  *     Attention tensors use the reference layout [B, H, N, D]
  *     (src/pallas_flash/ops/interface.py:27, kernels/decoding.py:111).
  *   - The caller owns every buffer.  No entry point allocates device memory
- *     or synchronises the host; all work is enqueued on `stream`
+ *     (except pu_peer_alloc, whose purpose is an IPC-exportable buffer) or
+ *     synchronises the host; all work is enqueued on `stream`
  *     (a cudaStream_t, NULL = legacy default stream).
  *   - Return value: PU_OK (0) or a PU_ERR_* code; pu_last_error() gives a
  *     human-readable message for the calling thread.
@@ -185,7 +186,8 @@ PU_API int pu_decode(const void* q, int q_dtype,
  *   Scratch: a fixed 8 MiB array in the library's device memory, present on
  *   every GPU that loads the library until the process exits.  A call needs
  *   256 KiB + B*H*splits*(D+2)*4 bytes (splits = the split count pu_decode
- *   chooses, about ceil(1184 / (B*H)) on a 148-SM B200); larger problems are
+ *   chooses on a 148-SM B200: floor(296 / (B*H)) without kv_lens, about
+ *   ceil(1184 / (B*H)) with kv_lens, at least 1); larger problems are
  *   rejected with PU_ERR_WORKSPACE and a message, before anything is enqueued.
  *   The entry point allocates nothing (no cudaMalloc/cudaFree, no library
  *   allocator); it clears the scratch counters with cudaMemsetAsync on
@@ -269,9 +271,9 @@ PU_API int pu_kv_append(const void* k_new, const void* v_new, int kv_dtype,
  * pu_peer_open.  Per decode step, every rank calls, on its own stream and
  * with the same epoch (1, 2, 3, ... in lockstep):
  *   pu_decode_push: the split-KV pass over the local shard; the record of
- *     each (b, h) is stored into every rank's exchange buffer and a flag is
- *     raised there.  exchange[g] = this process's pointer to rank g's buffer
- *     (its own allocation for g == rank).
+ *     each (b, h) is stored into every rank's exchange buffer as 64-bit
+ *     words {value, epoch}.  exchange[g] = this process's pointer to rank
+ *     g's buffer (its own allocation for g == rank).
  *   pu_decode_pull: waits until all G ranks have published this epoch
  *     (bounded by timeout_ns <= 2 s; on expiry pu_device_status reports
  *     PU_ERR_DEVICE_TIMEOUT, detail 304, and o is zeros), then merges the

@@ -459,10 +459,16 @@ struct Plan {
 
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms, long long align = 16) {
+// Split plan.  Without per-sequence lengths every (b, h) has the same work:
+// exactly one full wave of CTAs (splits = floor(resident CTAs / BH)) streams
+// best, since each CTA then pays its start-up and merge once.  With lengths
+// (ragged batches) the work per (b, h) is unknown on the host, so chunks are
+// finer (about kWaves waves) and CTAs past a sequence's end finish at once.
+inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms, bool ragged,
+                      long long align = 16) {
   Plan pl{};
-  const long long target = (long long)num_sms * kCtasPerSm * kWaves;
-  long long splits = (target + BH - 1) / BH;
+  const long long slots = (long long)num_sms * kCtasPerSm;
+  long long splits = ragged ? (slots * kWaves + BH - 1) / BH : std::max<long long>(1, slots / BH);
   const long long max_splits = std::max<long long>(1, (n_local + kMinChunk - 1) / kMinChunk);
   splits = std::max<long long>(1, std::min(splits, max_splits));
   long long chunk = (n_local + splits - 1) / splits;
@@ -473,6 +479,12 @@ inline Plan make_plan(long long BH, long long n_local, long long D, int num_sms,
   pl.rec_off = kCountBytes;
   pl.total_bytes = pl.rec_off + round_up((size_t)BH * splits * (D + 2) * sizeof(float), 256);
   return pl;
+}
+
+// Workspace that serves a call with or without lengths.
+inline size_t workspace_bytes_any(long long BH, long long n_local, long long D, int num_sms) {
+  return std::max(make_plan(BH, n_local, D, num_sms, false).total_bytes,
+                  make_plan(BH, n_local, D, num_sms, true).total_bytes);
 }
 
 template <bool kFinal, bool kPaged = false, bool kPush = false>
@@ -519,7 +531,7 @@ extern "C" {
 
 size_t pu_decode_workspace_size(int64_t B, int64_t H, int64_t n_local, int64_t D) {
   if (B <= 0 || H <= 0 || n_local <= 0 || D <= 0) return 0;
-  return pu::decode::make_plan(B * H, n_local, D, pu::sm_count()).total_bytes;
+  return pu::decode::workspace_bytes_any(B * H, n_local, D, pu::sm_count());
 }
 
 int pu_decode_partial(const void* q, int q_dtype, const void* k_cache, const void* v_cache,
@@ -531,7 +543,7 @@ int pu_decode_partial(const void* q, int q_dtype, const void* k_cache, const voi
   if (rc) return rc;
   if (!partial) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null partial output");
   if (kv_offset < 0) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "negative kv_offset");
-  const Plan pl = make_plan(B * H, n_local, D, pu::sm_count());
+  const Plan pl = make_plan(B * H, n_local, D, pu::sm_count(), kv_lens != nullptr);
   if (!workspace || workspace_bytes < pl.total_bytes)
     return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
                          workspace_bytes);
@@ -559,7 +571,7 @@ int pu_decode(const void* q, int q_dtype, const void* k_cache, const void* v_cac
   int rc = check_args(q, q_dtype, k_cache, v_cache, kv_dtype, B, H, n, D);
   if (rc) return rc;
   if (!o) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null output");
-  const Plan pl = make_plan(B * H, n, D, pu::sm_count());
+  const Plan pl = make_plan(B * H, n, D, pu::sm_count(), kv_lens != nullptr);
   if (!workspace || workspace_bytes < pl.total_bytes)
     return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
                          workspace_bytes);

@@ -82,7 +82,7 @@ inline int check_pages(const int32_t* table, long long max_pages, long long num_
 extern "C" size_t pu_decode_paged_workspace_size(int64_t B, int64_t H, int64_t max_pages_per_seq,
                                                  int64_t page_size, int64_t D) {
   if (B <= 0 || H <= 0 || max_pages_per_seq <= 0 || page_size <= 0 || D <= 0) return 0;
-  return pu::decode::make_plan(B * H, max_pages_per_seq * page_size, D, pu::sm_count(), page_size).total_bytes;
+  return pu::decode::make_plan(B * H, max_pages_per_seq * page_size, D, pu::sm_count(), true, page_size).total_bytes;
 }
 
 extern "C" int pu_decode_paged(const void* q, int q_dtype, const void* k_pool, const void* v_pool, int kv_dtype,
@@ -98,7 +98,7 @@ extern "C" int pu_decode_paged(const void* q, int q_dtype, const void* k_pool, c
   rc = pu::paged::check_pages(page_table, max_pages_per_seq, num_pages, page_size, &shift);
   if (rc) return rc;
   if (!o || !kv_lens) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null output or lengths");
-  const Plan pl = make_plan(B * H, n_cap, D, pu::sm_count(), page_size);
+  const Plan pl = make_plan(B * H, n_cap, D, pu::sm_count(), true, page_size);
   if (!workspace || workspace_bytes < pl.total_bytes)
     return pu::set_error(PU_ERR_WORKSPACE, "paged decode workspace needs %zu bytes, got %zu", pl.total_bytes,
                          workspace_bytes);

@@ -85,7 +85,7 @@ int pu_decode_push(const void* q, int q_dtype, const void* k_cache, const void* 
   if (rank < 0 || rank >= G) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "rank %lld of %lld", (long long)rank, (long long)G);
   if (epoch == 0) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "epochs start at 1");
   if (kv_offset < 0) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "negative kv_offset");
-  const Plan pl = make_plan(B * H, n_local, D, pu::sm_count());
+  const Plan pl = make_plan(B * H, n_local, D, pu::sm_count(), kv_lens != nullptr);
   if (!workspace || workspace_bytes < pl.total_bytes)
     return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
                          workspace_bytes);

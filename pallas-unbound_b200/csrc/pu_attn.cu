@@ -58,7 +58,7 @@ extern "C" int pu_decode_noalloc(const void* q, int q_dtype, const void* k_cache
   int rc = check_args(q, q_dtype, k_cache, v_cache, kv_dtype, B, H, n, D);
   if (rc) return rc;
   if (!o) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null output");
-  const Plan pl = make_plan(B * H, n, D, pu::sm_count());
+  const Plan pl = make_plan(B * H, n, D, pu::sm_count(), kv_lens != nullptr);
   if (pl.total_bytes > pu::noalloc::kScratchBytes)
     return pu::set_error(PU_ERR_WORKSPACE,
                          "pu_decode_noalloc: B*H=%lld with %d splits needs %zu bytes of scratch, above "
