@@ -303,6 +303,20 @@ PU_API int pu_decode_pull(const void* exchange, int64_t G, uint32_t epoch,
                           void* o, float* lse, int64_t B, int64_t H, int64_t D,
                           uint64_t timeout_ns, void* stream);
 
+/*
+ * One sharded decode step: pu_decode_push followed by the merge.  When B*H
+ * is at most half of the GPU's resident split-KV CTAs (148 on a B200) the
+ * merge runs inside the push kernel (the last CTA of each (b, h) waits for
+ * the other ranks' records), otherwise as pu_decode_pull.  Same results.
+ */
+PU_API int pu_decode_sharded(const void* q, int q_dtype,
+                             const void* k_cache, const void* v_cache, int kv_dtype,
+                             const int32_t* kv_lens, int64_t kv_offset,
+                             void* const* exchange, int64_t G, int64_t rank, uint32_t epoch,
+                             void* o, float* lse, void* workspace, size_t workspace_bytes,
+                             int64_t B, int64_t H, int64_t n_local, int64_t D,
+                             float sm_scale, uint64_t timeout_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

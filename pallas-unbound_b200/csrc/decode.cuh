@@ -66,6 +66,7 @@ struct Params {
   int n_peers;
   int rank;
   unsigned epoch;
+  uint64_t timeout_ns;   // bound of the fused merge's wait
 };
 
 template <typename T>
@@ -131,6 +132,75 @@ __device__ __forceinline__ void merge_records(const float* rec, int nrec, int st
     L += w * __ldcg(r + 1);
     O += w * __ldcg(r + 2 + d);
   }
+}
+
+// Push-mode merge for one (b, h): wait (bounded) until the words of every
+// rank's record in the local exchange buffer carry `epoch`, then merge in
+// rank order (the arithmetic of combine_kernel).  Called by every thread of
+// the block (d = thread index; threads d >= D only join the vote).  A wait
+// that runs out records PU_ERR_DEVICE_TIMEOUT (detail kSiteDecodePeer) and
+// the output is zeros.
+__device__ __forceinline__ bool ll_wait(const unsigned long long* w, unsigned epoch, uint64_t timeout_ns,
+                                        float& value) {
+  unsigned long long x = ld_volatile_u64(w);
+  if ((unsigned)(x >> 32) != epoch) {
+    const uint64_t t0 = global_timer_ns();
+    do {
+      if (global_timer_ns() - t0 > timeout_ns) return false;
+      x = ld_volatile_u64(w);
+    } while ((unsigned)(x >> 32) != epoch);
+  }
+  value = __uint_as_float((unsigned)x);
+  return true;
+}
+
+template <int D>
+__device__ __forceinline__ void peer_merge(const unsigned long long* exch, int G, int BH, int bh, unsigned epoch,
+                                           uint64_t timeout_ns, __nv_bfloat16* o, float* lse, int d) {
+  const unsigned long long* base = exch + (size_t)(epoch & 1u) * G * BH * (D + 2);
+  float mg[kMaxPeers], lg[kMaxPeers], og[kMaxPeers];
+  bool ok = true;
+#pragma unroll
+  for (int g = 0; g < kMaxPeers; ++g) {
+    mg[g] = -INFINITY;
+    lg[g] = 0.f;
+    og[g] = 0.f;
+    if (d < D && g < G && ok) {
+      const unsigned long long* r = base + ((size_t)g * BH + bh) * (D + 2);
+      ok = ll_wait(r, epoch, timeout_ns, mg[g]) && ll_wait(r + 1, epoch, timeout_ns, lg[g]) &&
+           ll_wait(r + 2 + d, epoch, timeout_ns, og[g]);
+    }
+  }
+  if (!__syncthreads_and(ok)) {
+    if (d == 0) record_device_error(PU_ERR_DEVICE_TIMEOUT, kSiteDecodePeer);
+    if (d < D) o[(size_t)bh * D + d] = __float2bfloat16_rn(0.f);
+    if (d == 0 && lse != nullptr) lse[bh] = -INFINITY;
+    return;
+  }
+  if (d >= D) return;
+  float M = -INFINITY;
+#pragma unroll
+  for (int g = 0; g < kMaxPeers; ++g) M = fmaxf(M, mg[g]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+#pragma unroll
+    for (int g = 0; g < kMaxPeers; ++g) {
+      if (g >= G || mg[g] == -INFINITY) continue;
+      const float w = ex2((mg[g] - M) * kLog2e);
+      L += w * lg[g];
+      O += w * og[g];
+    }
+  }
+  o[(size_t)bh * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+  if (d == 0 && lse != nullptr) lse[bh] = (L > 0.f) ? M + logf(L) : -INFINITY;
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) peer_combine_kernel(const unsigned long long* __restrict__ exch, int G,
+                                                         int BH, unsigned epoch, uint64_t timeout_ns,
+                                                         __nv_bfloat16* __restrict__ o,
+                                                         float* __restrict__ lse) {
+  peer_merge<D>(exch, G, BH, blockIdx.x, epoch, timeout_ns, o, lse, threadIdx.x);
 }
 
 // kFinal: write the bf16 output; else the shard partial (to `partial`, or to
@@ -356,68 +426,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
     }
   }
   if (tid == 0) p.ws_count[bh] = 0;  // leave the workspace zeroed for the next call
-}
-
-// Push-mode merge: wait (bounded) until the words of every rank's record for
-// this (b, h) carry `epoch`, then merge in rank order (the arithmetic of
-// combine_kernel).  A wait that runs out records PU_ERR_DEVICE_TIMEOUT
-// (detail kSiteDecodePeer) and the output is zeros.
-__device__ __forceinline__ bool ll_wait(const unsigned long long* w, unsigned epoch, uint64_t timeout_ns,
-                                        float& value) {
-  unsigned long long x = ld_volatile_u64(w);
-  if ((unsigned)(x >> 32) != epoch) {
-    const uint64_t t0 = global_timer_ns();
-    do {
-      if (global_timer_ns() - t0 > timeout_ns) return false;
-      x = ld_volatile_u64(w);
-    } while ((unsigned)(x >> 32) != epoch);
+  if constexpr (kPush) {
+    // fused merge (p.o set): this CTA waits for the other ranks' records of
+    // (b, h); the host enables it only while the waiting CTAs (at most B*H)
+    // leave most CTA slots free, so every rank's remaining CTAs still run
+    if (p.o != nullptr)
+      peer_merge<D>(p.peer_rec[p.rank], p.n_peers, gridDim.y, bh, p.epoch, p.timeout_ns, p.o, p.lse, tid);
   }
-  value = __uint_as_float((unsigned)x);
-  return true;
-}
-
-template <int D>
-__global__ void __launch_bounds__(D) peer_combine_kernel(const unsigned long long* __restrict__ exch, int G,
-                                                         int BH, unsigned epoch, uint64_t timeout_ns,
-                                                         __nv_bfloat16* __restrict__ o,
-                                                         float* __restrict__ lse) {
-  const int bh = blockIdx.x;
-  const int d = threadIdx.x;
-  const unsigned long long* base = exch + (size_t)(epoch & 1u) * G * BH * (D + 2);
-  float mg[kMaxPeers], lg[kMaxPeers], og[kMaxPeers];
-  bool ok = true;
-#pragma unroll
-  for (int g = 0; g < kMaxPeers; ++g) {
-    mg[g] = -INFINITY;
-    lg[g] = 0.f;
-    og[g] = 0.f;
-    if (g < G && ok) {
-      const unsigned long long* r = base + ((size_t)g * BH + bh) * (D + 2);
-      ok = ll_wait(r, epoch, timeout_ns, mg[g]) && ll_wait(r + 1, epoch, timeout_ns, lg[g]) &&
-           ll_wait(r + 2 + d, epoch, timeout_ns, og[g]);
-    }
-  }
-  if (!__syncthreads_and(ok)) {
-    if (d == 0) record_device_error(PU_ERR_DEVICE_TIMEOUT, kSiteDecodePeer);
-    o[(size_t)bh * D + d] = __float2bfloat16_rn(0.f);
-    if (d == 0 && lse != nullptr) lse[bh] = -INFINITY;
-    return;
-  }
-  float M = -INFINITY;
-#pragma unroll
-  for (int g = 0; g < kMaxPeers; ++g) M = fmaxf(M, mg[g]);
-  float L = 0.f, O = 0.f;
-  if (M != -INFINITY) {
-#pragma unroll
-    for (int g = 0; g < kMaxPeers; ++g) {
-      if (g >= G || mg[g] == -INFINITY) continue;
-      const float w = ex2((mg[g] - M) * kLog2e);
-      L += w * lg[g];
-      O += w * og[g];
-    }
-  }
-  o[(size_t)bh * D + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
-  if (d == 0 && lse != nullptr) lse[bh] = (L > 0.f) ? M + logf(L) : -INFINITY;
 }
 
 // Merge G gathered shard records {m (natural log), l, o[D]} per (b, h).

@@ -73,22 +73,28 @@ size_t pu_decode_exchange_bytes(int64_t B, int64_t H, int64_t D, int64_t G) {
   return pu::peer::exchange_bytes(B * H, D, G);
 }
 
-int pu_decode_push(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
-                   const int32_t* kv_lens, int64_t kv_offset, void* const* exchange, int64_t G,
-                   int64_t rank, uint32_t epoch, void* workspace, size_t workspace_bytes, int64_t B,
-                   int64_t H, int64_t n_local, int64_t D, float sm_scale, void* stream) {
+}  // extern "C"
+
+namespace pu {
+namespace peer {
+
+// The split-KV pass in push mode; with `o` set, its last CTAs also wait for
+// and merge the other ranks' records (fused step).
+inline int push(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
+                const int32_t* kv_lens, int64_t kv_offset, void* const* exchange, int64_t G, int64_t rank,
+                uint32_t epoch, void* o, float* lse, uint64_t timeout_ns, void* workspace, size_t workspace_bytes,
+                int64_t B, int64_t H, int64_t n_local, int64_t D, float sm_scale, void* stream) {
   using namespace pu::decode;
   int rc = check_args(q, q_dtype, k_cache, v_cache, kv_dtype, B, H, n_local, D);
   if (rc) return rc;
-  if (!exchange) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null exchange pointer array");
-  if (G < 1 || G > kMaxPeers) return pu::set_error(PU_ERR_UNSUPPORTED, "%lld ranks (1..%d)", (long long)G, kMaxPeers);
-  if (rank < 0 || rank >= G) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "rank %lld of %lld", (long long)rank, (long long)G);
-  if (epoch == 0) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "epochs start at 1");
-  if (kv_offset < 0) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "negative kv_offset");
-  const Plan pl = make_plan(B * H, n_local, D, pu::sm_count(), kv_lens != nullptr);
+  if (!exchange) return set_error(PU_ERR_INVALID_ARGUMENT, "null exchange pointer array");
+  if (G < 1 || G > kMaxPeers) return set_error(PU_ERR_UNSUPPORTED, "%lld ranks (1..%d)", (long long)G, kMaxPeers);
+  if (rank < 0 || rank >= G) return set_error(PU_ERR_INVALID_ARGUMENT, "rank %lld of %lld", (long long)rank, (long long)G);
+  if (epoch == 0) return set_error(PU_ERR_INVALID_ARGUMENT, "epochs start at 1");
+  if (kv_offset < 0) return set_error(PU_ERR_INVALID_ARGUMENT, "negative kv_offset");
+  const Plan pl = make_plan(B * H, n_local, D, sm_count(), kv_lens != nullptr);
   if (!workspace || workspace_bytes < pl.total_bytes)
-    return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
-                         workspace_bytes);
+    return set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes, workspace_bytes);
   Params prm{};
   prm.q = q;
   prm.k = k_cache;
@@ -103,14 +109,36 @@ int pu_decode_push(const void* q, int q_dtype, const void* k_cache, const void* 
   prm.ws_rec = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.rec_off);
   prm.ws_count = static_cast<int*>(workspace);
   for (int g = 0; g < G; ++g) {
-    if (!exchange[g] || !pu::aligned16(exchange[g]))
-      return pu::set_error(PU_ERR_INVALID_ARGUMENT, "exchange buffer %d null or unaligned", g);
+    if (!exchange[g] || !aligned16(exchange[g]))
+      return set_error(PU_ERR_INVALID_ARGUMENT, "exchange buffer %d null or unaligned", g);
     prm.peer_rec[g] = static_cast<unsigned long long*>(exchange[g]);
   }
   prm.n_peers = (int)G;
   prm.rank = (int)rank;
   prm.epoch = epoch;
+  prm.o = static_cast<__nv_bfloat16*>(o);
+  prm.lse = lse;
+  prm.timeout_ns = timeout_ns;
   return launch<false, false, true>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));
+}
+
+inline int check_timeout(uint64_t timeout_ns) {
+  if (timeout_ns == 0 || timeout_ns > kWaitTimeoutNs)
+    return set_error(PU_ERR_INVALID_ARGUMENT, "timeout must be in (0, 2 s]");
+  return PU_OK;
+}
+
+}  // namespace peer
+}  // namespace pu
+
+extern "C" {
+
+int pu_decode_push(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
+                   const int32_t* kv_lens, int64_t kv_offset, void* const* exchange, int64_t G,
+                   int64_t rank, uint32_t epoch, void* workspace, size_t workspace_bytes, int64_t B,
+                   int64_t H, int64_t n_local, int64_t D, float sm_scale, void* stream) {
+  return pu::peer::push(q, q_dtype, k_cache, v_cache, kv_dtype, kv_lens, kv_offset, exchange, G, rank, epoch,
+                        nullptr, nullptr, 0, workspace, workspace_bytes, B, H, n_local, D, sm_scale, stream);
 }
 
 int pu_decode_pull(const void* exchange, int64_t G, uint32_t epoch, void* o, float* lse, int64_t B, int64_t H,
@@ -120,8 +148,7 @@ int pu_decode_pull(const void* exchange, int64_t G, uint32_t epoch, void* o, flo
   if (D != 64 && D != 128) return pu::set_error(PU_ERR_UNSUPPORTED, "head size %lld", (long long)D);
   if (B <= 0 || H <= 0 || B * H > pu::decode::kMaxBH) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "bad B*H");
   if (epoch == 0) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "epochs start at 1");
-  if (timeout_ns == 0 || timeout_ns > pu::kWaitTimeoutNs)
-    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "timeout must be in (0, 2 s]");
+  if (int rc = pu::peer::check_timeout(timeout_ns)) return rc;
   if (!pu::aligned16(exchange)) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "exchange buffer unaligned");
   const auto* words = static_cast<const unsigned long long*>(exchange);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -133,6 +160,25 @@ int pu_decode_pull(const void* exchange, int64_t G, uint32_t epoch, void* o, flo
     pu::decode::peer_combine_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(words, (int)G, (int)(B * H), epoch,
                                                                          timeout_ns, out, lse);
   return pu::check_cuda(cudaGetLastError(), "peer combine launch");
+}
+
+int pu_decode_sharded(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
+                      const int32_t* kv_lens, int64_t kv_offset, void* const* exchange, int64_t G, int64_t rank,
+                      uint32_t epoch, void* o, float* lse, void* workspace, size_t workspace_bytes, int64_t B,
+                      int64_t H, int64_t n_local, int64_t D, float sm_scale, uint64_t timeout_ns, void* stream) {
+  if (!o) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null output");
+  if (int rc = pu::peer::check_timeout(timeout_ns)) return rc;
+  // The fused merge makes the last CTA of each (b, h) wait for the other
+  // ranks; with at most half of the resident CTA slots waiting, every rank's
+  // other CTAs always find room to run.
+  const long long slots = (long long)pu::sm_count() * pu::decode::kCtasPerSm;
+  if (2 * B * H <= slots)
+    return pu::peer::push(q, q_dtype, k_cache, v_cache, kv_dtype, kv_lens, kv_offset, exchange, G, rank, epoch, o,
+                          lse, timeout_ns, workspace, workspace_bytes, B, H, n_local, D, sm_scale, stream);
+  int rc = pu::peer::push(q, q_dtype, k_cache, v_cache, kv_dtype, kv_lens, kv_offset, exchange, G, rank, epoch,
+                          nullptr, nullptr, 0, workspace, workspace_bytes, B, H, n_local, D, sm_scale, stream);
+  if (rc) return rc;
+  return pu_decode_pull(exchange[rank], G, epoch, o, lse, B, H, D, timeout_ns, stream);
 }
 
 }  // extern "C"

@@ -68,6 +68,10 @@ SIGNATURES = {
                               _i64, _i64, _i64, _i64, _float, _c_void_p]),
     "pu_decode_pull": (_int, [_c_void_p, _i64, ctypes.c_uint32, _c_void_p, _c_void_p, _i64,
                               _i64, _i64, ctypes.c_uint64, _c_void_p]),
+    "pu_decode_sharded": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _i64,
+                                 _c_void_p, _i64, _i64, ctypes.c_uint32, _c_void_p, _c_void_p,
+                                 _c_void_p, _size_t, _i64, _i64, _i64, _i64, _float,
+                                 ctypes.c_uint64, _c_void_p]),
     "pu_kv_append": (_int, [_c_void_p, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p, _i64,
                             _i64, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p]),
 }

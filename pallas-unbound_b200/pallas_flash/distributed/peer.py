@@ -4,11 +4,12 @@ Replaces the all-gather of the packed (m, l, o) partials
 (`collectives.all_gather_partials`) with direct peer stores: every rank
 allocates one exchange buffer (pu_peer_alloc), the IPC handles are shared
 once over the process group, and each rank maps the others' buffers
-(pu_peer_open).  A decode step is then two kernels per rank and no
-collective: pu_decode_push (split-KV pass; each (b, h) record stored into
-every rank's buffer, flag raised) and pu_decode_pull (bounded wait for the
-G flags, stable LogSumExp merge).  The merge the reference documents for its
-sharded decode is a psum of LogSumExp terms (README.md:41-46).
+(pu_peer_open).  A decode step is then one or two kernels per rank and no
+collective: pu_decode_sharded (the split-KV pass stores each (b, h) record
+into every rank's buffer as epoch-tagged words; a bounded wait for the G
+records and the stable LogSumExp merge follow, inside the same kernel for
+small B*H, else as a second kernel).  The merge the reference documents
+for its sharded decode is a psum of LogSumExp terms (README.md:41-46).
 
 All ranks must call `decode` the same number of times (the epoch counter
 advances in lockstep); `close()` is collective.
@@ -80,17 +81,16 @@ class PeerExchange:
         if self.epoch >= 2 ** 31:
             raise RuntimeError("epoch counter exhausted; create a new exchange")
         n_local = k_shard.shape[2]
-        _lib.check(lib.pu_decode_push(q.data_ptr(), _DT[q.dtype], k_shard.data_ptr(),
-                                      v_shard.data_ptr(), _DT[k_shard.dtype],
-                                      kv_lens.data_ptr() if kv_lens is not None else None,
-                                      int(kv_offset), self._ptrs, self.world, self.rank,
-                                      self.epoch, workspace.data_ptr(), workspace.numel(), B, H,
-                                      n_local, D, float(sm_scale), stream), "pu_decode_push")
         o = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device=q.device)
         lse = torch.empty((B, H), dtype=torch.float32, device=q.device)
-        _lib.check(lib.pu_decode_pull(self._local, self.world, self.epoch, o.data_ptr(),
-                                      lse.data_ptr(), B, H, D, int(timeout_ns), stream),
-                   "pu_decode_pull")
+        _lib.check(lib.pu_decode_sharded(q.data_ptr(), _DT[q.dtype], k_shard.data_ptr(),
+                                         v_shard.data_ptr(), _DT[k_shard.dtype],
+                                         kv_lens.data_ptr() if kv_lens is not None else None,
+                                         int(kv_offset), self._ptrs, self.world, self.rank,
+                                         self.epoch, o.data_ptr(), lse.data_ptr(),
+                                         workspace.data_ptr(), workspace.numel(), B, H, n_local, D,
+                                         float(sm_scale), int(timeout_ns), stream),
+                   "pu_decode_sharded")
         return o, lse
 
     def _release(self):

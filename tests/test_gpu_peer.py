@@ -56,6 +56,23 @@ def test_push_pull_equals_partial_combine(group):
     assert _lib.device_status() == (0, 0)
 
 
+def test_unfused_merge_for_large_batches(group):
+    """B*H above half the CTA slots: the merge runs as a second kernel."""
+    from pallas_flash import _lib
+    from pallas_flash.kernels import decoding as dec
+    B, H, N, D = 5, 32, 600, 64
+    k = _gen((B, H, N, D), 21)
+    v = _gen((B, H, N, D), 22)
+    for step in range(3):
+        q = _gen((B, H, 1, D), 30 + step)
+        part = dec.decode_partial(q, k, v, kv_offset=0)
+        o_ref, l_ref = dec.decode_combine(part[None], B, H, D)
+        o, l = dec.pallas_flash_decoding(q, k, v, group=group, transport="peer", return_lse=True)
+        torch.cuda.synchronize()
+        assert torch.equal(o, o_ref) and torch.equal(l, l_ref), step
+    assert _lib.device_status() == (0, 0)
+
+
 def test_pull_wait_runs_out(group):
     """A merge for an epoch nobody publishes gives up after its limit,
     reports PU_ERR_DEVICE_TIMEOUT / 304, and later steps still work."""
