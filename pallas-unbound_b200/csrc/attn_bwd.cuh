@@ -47,7 +47,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;
 
 struct Params {
-  int Nq, Nkv, H;
+  int Nq, Nkv, H, BH;
   int n_q_tiles, n_kv_tiles;
   int causal;
   float scale_log2;
@@ -146,10 +146,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bFinal + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  // blockIdx.x walks the key tiles of one (b, h) — heaviest (causal: first)
-  // first — and blockIdx.y the (b, h).
-  const int kv_tile = blockIdx.x;
-  const int bh = blockIdx.y;
+  // One linear grid, (b, h) fastest: all heads' heaviest (causal: first)
+  // key tiles first (longest-first start order).
+  const int kv_tile = (int)(blockIdx.x / (unsigned)p.BH);
+  const int bh = (int)(blockIdx.x % (unsigned)p.BH);
   const int kv0 = kv_tile * BN;
   const int first_q = p.causal ? min(kv0 / BM, p.n_q_tiles) : 0;
   const int n_it = p.n_q_tiles - first_q;
@@ -442,9 +442,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bDQd + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  // heaviest (causal: last) query tiles first
-  const int q_tile = p.n_q_tiles - 1 - (int)blockIdx.x;
-  const int bh = blockIdx.y;
+  // one linear grid, (b, h) fastest, heaviest (causal: last) query tiles first
+  const int q_tile = p.n_q_tiles - 1 - (int)(blockIdx.x / (unsigned)p.BH);
+  const int bh = (int)(blockIdx.x % (unsigned)p.BH);
   const int q0 = q_tile * BM;
   int n_blocks = p.n_kv_tiles;
   if (p.causal) n_blocks = max(1, min(n_blocks, (q0 + BM + BN - 1) / BN));
@@ -738,6 +738,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
   prm.Nq = (int)Nq;
   prm.Nkv = (int)Nkv;
   prm.H = (int)H;
+  prm.BH = (int)BH;
   prm.n_q_tiles = (int)((Nq + BM - 1) / BM);
   prm.n_kv_tiles = (int)((Nkv + BN - 1) / BN);
   prm.causal = causal ? 1 : 0;
@@ -749,11 +750,11 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
   prm.dq = static_cast<__nv_bfloat16*>(dq);
   prm.dk = static_cast<__nv_bfloat16*>(dk);
   prm.dv = static_cast<__nv_bfloat16*>(dv);
-  attn_bwd_dkdv_kernel<D><<<dim3((unsigned)prm.n_kv_tiles, (unsigned)BH), kThreads, CfgKV<D>::kSmemBytes, st>>>(
+  attn_bwd_dkdv_kernel<D><<<dim3((unsigned)((long long)prm.n_kv_tiles * BH)), kThreads, CfgKV<D>::kSmemBytes, st>>>(
       tq, tk, tv, tdo, prm);
   rc = check_cuda(cudaGetLastError(), "backward dK/dV launch");
   if (rc) return rc;
-  attn_bwd_dq_kernel<D><<<dim3((unsigned)prm.n_q_tiles, (unsigned)BH), kThreads, CfgQ<D>::kSmemBytes, st>>>(
+  attn_bwd_dq_kernel<D><<<dim3((unsigned)((long long)prm.n_q_tiles * BH)), kThreads, CfgQ<D>::kSmemBytes, st>>>(
       tq, tk, tv, tdo, prm);
   return check_cuda(cudaGetLastError(), "backward dQ launch");
 }

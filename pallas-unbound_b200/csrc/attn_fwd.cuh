@@ -69,6 +69,7 @@ struct Cfg {
 struct Params {
   int Nq, Nkv, H;
   int n_q_pairs;       // CTAs per (b, h): ceil(Nq / 256)
+  int BH;
   int causal;
   float scale_log2;
   __nv_bfloat16* o;
@@ -103,10 +104,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bOf + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  // blockIdx.x walks the 256-row query blocks of one (b, h) — heaviest
-  // (causal: last) first — and blockIdx.y the (b, h).
-  const int bh = blockIdx.y;
-  const int q0 = (p.n_q_pairs - 1 - (int)blockIdx.x) * (2 * BM);
+  // One linear grid, (b, h) fastest: all heads' heaviest (causal: last)
+  // 256-row query blocks first, so CTAs start longest-first and the last
+  // wave holds only the lightest blocks.
+  const int bh = (int)(blockIdx.x % (unsigned)p.BH);
+  const int q0 = (p.n_q_pairs - 1 - (int)(blockIdx.x / (unsigned)p.BH)) * (2 * BM);
   const int n_kv_total = (p.Nkv + BN - 1) / BN;
   int n_t[2];
 #pragma unroll
@@ -374,6 +376,8 @@ inline int check_common(const void* q, const void* k, const void* v, long long B
   if (B * H > 65535) return set_error(PU_ERR_UNSUPPORTED, "B*H = %lld exceeds 65535", B * H);
   if (Nq > (1ll << 24) || Nkv > (1ll << 24))
     return set_error(PU_ERR_UNSUPPORTED, "sequence length above 2^24");
+  if (((std::max(Nq, Nkv) + 127) / 128) * B * H > 0x7fffffffll)
+    return set_error(PU_ERR_UNSUPPORTED, "B*H*ceil(N/128) above 2^31 - 1");
   return PU_OK;
 }
 
@@ -405,7 +409,8 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   prm.scale_log2 = sm_scale * kLog2e;
   prm.o = static_cast<__nv_bfloat16*>(o);
   prm.lse = lse;
-  dim3 grid((unsigned)prm.n_q_pairs, (unsigned)(B * H));
+  prm.BH = (int)(B * H);
+  dim3 grid((unsigned)((long long)prm.n_q_pairs * B * H));
   attn_fwd_kernel<D><<<grid, kThreads, C::kSmemBytes, st>>>(tq, tk, tv, prm);
   return check_cuda(cudaGetLastError(), "attention forward launch");
 }
