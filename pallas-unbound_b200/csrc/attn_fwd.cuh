@@ -6,8 +6,14 @@
 // walks 128-row K/V blocks with an fp32 online softmax, P rounded to bf16
 // (low_level/intrinsics.py:33-37) before the P.V product.
 //
-// B200 design: one CTA owns two 128-row query tiles (256 rows) of one (b, h)
-// and streams every K/V block once for both.
+// B200 design: a persistent grid (one CTA per SM) walks work items of two
+// 128-row query tiles (256 rows) of one (b, h); each item streams every K/V
+// block once for both tiles.  Items are ordered longest first (causal: the
+// last query blocks) with (b, h) fastest, and dealt to the CTAs in snake
+// order (round r: CTA c takes item r*G + c, or r*G + G-1-c for odd r), which
+// balances the causal work.  The rings, barriers and TMEM carry over from one
+// item to the next, so item r+1's Q load and first QK^T products overlap
+// item r's last products and epilogue.
 //   warp 8      TMA producer: Q tiles once, then K_j / V_j through NS-deep
 //               rings of 128-row tiles (128-byte swizzle).
 //   warp 9      tcgen05 issuer (one thread) and TMEM owner.  Per K/V block j:
@@ -61,15 +67,17 @@ struct Cfg {
   static constexpr int kOffV = kOffK + NS * kTileKV;
   static constexpr int kOffBar = kOffV + NS * kTileKV;
   // barriers: Q_full[2], K_full[NS], K_empty[NS], V_full[NS], V_empty[NS],
-  //           S_full[2], P_full[2], O_final[2]; then tmem base + abort flag
-  static constexpr int kNumBars = 2 + 4 * NS + 6;
+  //           S_full[2], P_full[2], O_final[2], Q_empty[2]; then tmem base +
+  //           abort flag
+  static constexpr int kNumBars = 2 + 4 * NS + 8;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
 };
 
 struct Params {
   int Nq, Nkv, H;
-  int n_q_pairs;       // CTAs per (b, h): ceil(Nq / 256)
+  int n_q_pairs;       // work items per (b, h): ceil(Nq / 256)
   int BH;
+  int n_items;         // n_q_pairs * BH
   int causal;
   float scale_log2;
   __nv_bfloat16* o;
@@ -101,22 +109,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bS = bVe + C::NS;       // [2]
   uint64_t* bP = bS + 2;            // [2]
   uint64_t* bOf = bP + 2;           // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bOf + 2);
+  uint64_t* bQe = bOf + 2;          // [2] Q tile t no longer read (last S_t done)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bQe + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  // One linear grid, (b, h) fastest: all heads' heaviest (causal: last)
-  // 256-row query blocks first, so CTAs start longest-first and the last
-  // wave holds only the lightest blocks.
-  const int bh = (int)(blockIdx.x % (unsigned)p.BH);
-  const int q0 = (p.n_q_pairs - 1 - (int)(blockIdx.x / (unsigned)p.BH)) * (2 * BM);
+  // Work item of round r for this CTA (snake order), or -1 when done; an
+  // item is (b, h) = L % BH and query block n_q_pairs - 1 - L / BH.
+  const int G = (int)gridDim.x;
+  const int cta = (int)blockIdx.x;
+  auto item_of = [&](int r) -> int {
+    const long long L = (long long)r * G + ((r & 1) ? (G - 1 - cta) : cta);
+    return L < p.n_items ? (int)L : -1;
+  };
   const int n_kv_total = (p.Nkv + BN - 1) / BN;
-  int n_t[2];
+  // K/V blocks each query tile of item L visits
+  auto blocks_of = [&](int L, int (&n_t)[2]) {
+    const int q0 = (p.n_q_pairs - 1 - L / p.BH) * (2 * BM);
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    n_t[t] = n_kv_total;
-    if (p.causal) n_t[t] = max(1, min(n_kv_total, (q0 + t * BM + BM + BN - 1) / BN));
-  }
-  const int n_max = max(n_t[0], n_t[1]);
+    for (int t = 0; t < 2; ++t) {
+      n_t[t] = n_kv_total;
+      if (p.causal) n_t[t] = max(1, min(n_kv_total, (q0 + t * BM + BM + BN - 1) / BN));
+    }
+    return q0;
+  };
 
   if (tid == 0) {
     for (int t = 0; t < 2; ++t) {
@@ -124,6 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bS + t, 1);
       mbar_init(bP + t, 128);
       mbar_init(bOf + t, 1);
+      mbar_init(bQe + t, 1);
     }
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(bKf + s, 1);
@@ -149,22 +165,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      for (int t = 0; t < 2; ++t) {
-        mbar_arrive_expect_tx(bQ + t, C::kTileQ);
-        for (int cb = 0; cb < C::kColBlocks; ++cb)
-          tma_load_3d(sQ + t * C::kTileQ + cb * BM * 128, &tmQ, bQ + t, cb * 64, q0 + t * BM, bh);
-      }
-      for (int j = 0; j < n_max; ++j) {
-        const int st = j % C::NS;
-        const uint32_t u = j / C::NS;
-        if (u > 0 && !mbar_wait(bKe + st, (u - 1) & 1, abort_flag, kSiteFwdKEmpty)) break;
-        mbar_arrive_expect_tx(bKf + st, C::kTileKV);
-        for (int cb = 0; cb < C::kColBlocks; ++cb)
-          tma_load_3d(sK + st * C::kTileKV + cb * BN * 128, &tmK, bKf + st, cb * 64, j * BN, bh);
-        if (u > 0 && !mbar_wait(bVe + st, (u - 1) & 1, abort_flag, kSiteFwdVEmpty)) break;
-        mbar_arrive_expect_tx(bVf + st, C::kTileKV);
-        for (int cb = 0; cb < C::kColBlocks; ++cb)
-          tma_load_3d(sV + st * C::kTileKV + cb * BN * 128, &tmV, bVf + st, cb * 64, j * BN, bh);
+      bool ok = true;
+      int jg = 0;                                       // K/V blocks loaded so far
+      for (int r = 0; ok; ++r) {
+        const int L = item_of(r);
+        if (L < 0) break;
+        const int bh = L % p.BH;
+        int n_t[2];
+        const int q0 = blocks_of(L, n_t);
+        const int n_max = max(n_t[0], n_t[1]);
+        for (int t = 0; t < 2; ++t) {
+          if (r > 0 && !mbar_wait(bQe + t, (r - 1) & 1, abort_flag, kSiteFwdQ)) { ok = false; break; }
+          mbar_arrive_expect_tx(bQ + t, C::kTileQ);
+          for (int cb = 0; cb < C::kColBlocks; ++cb)
+            tma_load_3d(sQ + t * C::kTileQ + cb * BM * 128, &tmQ, bQ + t, cb * 64, q0 + t * BM, bh);
+        }
+        for (int j = 0; ok && j < n_max; ++j, ++jg) {
+          const int st = jg % C::NS;
+          const uint32_t u = jg / C::NS;
+          if (u > 0 && !mbar_wait(bKe + st, (u - 1) & 1, abort_flag, kSiteFwdKEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(bKf + st, C::kTileKV);
+          for (int cb = 0; cb < C::kColBlocks; ++cb)
+            tma_load_3d(sK + st * C::kTileKV + cb * BN * 128, &tmK, bKf + st, cb * 64, j * BN, bh);
+          if (u > 0 && !mbar_wait(bVe + st, (u - 1) & 1, abort_flag, kSiteFwdVEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(bVf + st, C::kTileKV);
+          for (int cb = 0; cb < C::kColBlocks; ++cb)
+            tma_load_3d(sV + st * C::kTileKV + cb * BN * 128, &tmV, bVf + st, cb * 64, j * BN, bh);
+        }
       }
     }
   } else if (warp == 9) {
@@ -176,9 +203,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dQ0 = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t dK0 = make_sdesc_sw128(smem_u32(sK), 16, 1024);
       const uint64_t dV0 = make_sdesc_sw128(smem_u32(sV), BN * 128, 1024);
-      auto issue_S = [&](int t, int j) {
+      // S_t = Q_t K^T with K in ring slot `slot`
+      auto issue_S = [&](int t, int slot) {
         const uint64_t dq = sdesc_add(dQ0, t * C::kTileQ);
-        const uint64_t dk = sdesc_add(dK0, (j % C::NS) * C::kTileKV);
+        const uint64_t dk = sdesc_add(dK0, slot * C::kTileKV);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
@@ -187,64 +215,86 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bS + t);
       };
-      auto issue_PV = [&](int t, int j) {
-        const uint64_t dv = sdesc_add(dV0, (j % C::NS) * C::kTileKV);
+      // O_t (+)= P_t V with V in ring slot `slot`
+      auto issue_PV = [&](int t, int slot, bool first) {
+        const uint64_t dv = sdesc_add(dV0, slot * C::kTileKV);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           mma_ts(tmem + col_o(t), tmem + col_s(t) + kk * 8, sdesc_add(dv, kk * 16 * 128), idO,
-                 (j > 0 || kk > 0));
+                 (!first || kk > 0));
         }
       };
-      bool ok = mbar_wait(bKf, 0, abort_flag, kSiteFwdKFull);
-      for (int t = 0; ok && t < 2; ++t) {
-        ok = mbar_wait(bQ + t, 0, abort_flag, kSiteFwdQ);
-        if (!ok) break;
-        tc_fence_after();
-        issue_S(t, 0);
-      }
-      if (ok) mma_commit(bKe);
-      for (int j = 0; ok && j < n_max; ++j) {
-        const int st = j % C::NS;
-        const int nst = (j + 1) % C::NS;
-        if (!mbar_wait(bVf + st, (j / C::NS) & 1, abort_flag, kSiteFwdVFull)) break;
-        const bool next_k = (j + 1 < n_max);
-        bool k_ready = false;
-        for (int t = 0; t < 2; ++t) {
-          if (j >= n_t[t]) continue;
-          if (!mbar_wait(bP + t, j & 1, abort_flag, kSiteFwdPFull)) { ok = false; break; }
+      bool ok = true;
+      int jg = 0;                                       // K/V blocks consumed so far
+      uint32_t jp[2] = {0, 0};                          // P_t blocks consumed so far
+      for (int r = 0; ok; ++r) {
+        const int L = item_of(r);
+        if (L < 0) break;
+        int n_t[2];
+        blocks_of(L, n_t);
+        const int n_max = max(n_t[0], n_t[1]);
+        ok = mbar_wait(bKf + jg % C::NS, (jg / C::NS) & 1, abort_flag, kSiteFwdKFull);
+        for (int t = 0; ok && t < 2; ++t) {
+          ok = mbar_wait(bQ + t, r & 1, abort_flag, kSiteFwdQ);
+          if (!ok) break;
           tc_fence_after();
-          issue_PV(t, j);
-          if (j + 1 < n_t[t]) {
-            if (!k_ready) {
-              if (!mbar_wait(bKf + nst, ((j + 1) / C::NS) & 1, abort_flag, kSiteFwdKFull)) { ok = false; break; }
-              tc_fence_after();
-              k_ready = true;
-            }
-            issue_S(t, j + 1);
-          } else {
-            mma_commit(bOf + t);
-          }
+          issue_S(t, jg % C::NS);
+          if (n_t[t] == 1) mma_commit(bQe + t);         // Q_t's last reader
         }
-        if (!ok) break;
-        mma_commit(bVe + st);
-        if (next_k) mma_commit(bKe + nst);
+        if (ok) mma_commit(bKe + jg % C::NS);
+        for (int j = 0; ok && j < n_max; ++j) {
+          const int st = (jg + j) % C::NS;
+          const int nst = (jg + j + 1) % C::NS;
+          if (!mbar_wait(bVf + st, ((jg + j) / C::NS) & 1, abort_flag, kSiteFwdVFull)) { ok = false; break; }
+          const bool next_k = (j + 1 < n_max);
+          bool k_ready = false;
+          for (int t = 0; t < 2; ++t) {
+            if (j >= n_t[t]) continue;
+            if (!mbar_wait(bP + t, jp[t] & 1, abort_flag, kSiteFwdPFull)) { ok = false; break; }
+            ++jp[t];
+            tc_fence_after();
+            issue_PV(t, st, j == 0);
+            if (j + 1 < n_t[t]) {
+              if (!k_ready) {
+                if (!mbar_wait(bKf + nst, ((jg + j + 1) / C::NS) & 1, abort_flag, kSiteFwdKFull)) { ok = false; break; }
+                tc_fence_after();
+                k_ready = true;
+              }
+              issue_S(t, nst);
+              if (j + 2 == n_t[t]) mma_commit(bQe + t);  // Q_t's last reader
+            } else {
+              mma_commit(bOf + t);
+            }
+          }
+          if (!ok) break;
+          mma_commit(bVe + st);
+          if (next_k) mma_commit(bKe + nst);
+        }
+        jg += n_max;
       }
     }
   } else {
     // ---------------- softmax warpgroups (warps 0-3: tile 0, 4-7: tile 1) ----------------
     const int t = warp >> 2;
     const int row = tid & 127;                 // TMEM lane == query row in tile
-    const int q_tile0 = q0 + t * BM;
-    const int q_idx = q_tile0 + row;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_base + col_s(t);
     const uint32_t tO = tmem + lane_base + col_o(t);
+    bool ok = true;
+    uint32_t js = 0;                           // S_t blocks consumed so far
+    for (int r = 0; ok; ++r) {
+    const int L = item_of(r);
+    if (L < 0) break;
+    const int bh = L % p.BH;
+    int n_t[2];
+    const int q0 = blocks_of(L, n_t);
+    const int q_tile0 = q0 + t * BM;
+    const int q_idx = q_tile0 + row;
     const int n_blocks = n_t[t];
     float m_ref = -INFINITY;                   // log2 domain
     float l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_blocks; ++j) {
-      ok = mbar_wait(bS + t, j & 1, abort_flag, kSiteFwdSFull);
+    for (int j = 0; j < n_blocks; ++j, ++js) {
+      ok = mbar_wait(bS + t, js & 1, abort_flag, kSiteFwdSFull);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
@@ -287,13 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tO + c * 32, r);
+          uint32_t ov[32];
+          tmem_ld32(tO + c * 32, ov);
           tmem_wait_ld();
-          reg_fence(r);
+          reg_fence(ov);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(tO + c * 32, r);
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st32(tO + c * 32, ov);
         }
       }
       // P = 2^(s*scale - m): scale-subtract and row sum on pairs of scores in
@@ -328,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(bP + t);
     }
     if (ok) {
-      ok = mbar_wait(bOf + t, 0, abort_flag, kSiteFwdODone);
+      ok = mbar_wait(bOf + t, r & 1, abort_flag, kSiteFwdODone);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
@@ -337,15 +387,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       __nv_bfloat16* orow = p.o + ((size_t)bh * p.Nq + q_idx) * D;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tO + c * 32, r);
+        uint32_t ov[32];
+        tmem_ld32(tO + c * 32, ov);
         tmem_wait_ld();
-        reg_fence(r);
+        reg_fence(ov);
         if (q_idx < p.Nq) {
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            w[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv_l, __uint_as_float(r[2 * i + 1]) * inv_l);
+            w[i] = pack_bf16x2(__uint_as_float(ov[2 * i]) * inv_l, __uint_as_float(ov[2 * i + 1]) * inv_l);
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
@@ -355,8 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         p.lse[(size_t)bh * p.Nq + q_idx] = (m_ref + lg2(l)) * kLn2;
       }
     }
+    }  // items
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {
@@ -410,7 +460,8 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   prm.o = static_cast<__nv_bfloat16*>(o);
   prm.lse = lse;
   prm.BH = (int)(B * H);
-  dim3 grid((unsigned)((long long)prm.n_q_pairs * B * H));
+  prm.n_items = (int)((long long)prm.n_q_pairs * B * H);
+  dim3 grid((unsigned)std::min<long long>(prm.n_items, sm_count()));
   attn_fwd_kernel<D><<<grid, kThreads, C::kSmemBytes, st>>>(tq, tk, tv, prm);
   return check_cuda(cudaGetLastError(), "attention forward launch");
 }
