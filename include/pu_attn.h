@@ -51,6 +51,7 @@ extern "C" {
 #define PU_DTYPE_BF16 0
 #define PU_DTYPE_F16 1
 #define PU_DTYPE_F32 2
+#define PU_DTYPE_FP8_E4M3 3   /* KV caches of pu_decode_gqa only */
 
 /* Number of floats in one packed split-KV partial record: m, l, o[D]. */
 #define PU_PARTIAL_FLOATS(D) ((D) + 2)
@@ -175,6 +176,26 @@ PU_API int pu_decode(const void* q, int q_dtype,
               void* workspace, size_t workspace_bytes,
               int64_t B, int64_t H, int64_t n, int64_t D,
               float sm_scale, void* stream);
+
+/*
+ * Single-GPU decode step with grouped K/V heads and optional fp8 caches.
+ * No counterpart in the reference (its decode has one K/V head per query
+ * head and a bf16 cache, kernels/decoding.py:105-115); same step as
+ * pu_decode otherwise.
+ *   q [B,H,1,D] f16/bf16; k_cache/v_cache [B,H_kv,n,D] with H % H_kv == 0:
+ *   query head h reads K/V head h / (H / H_kv) (GQA; H_kv = 1 is MQA).
+ *   kv_dtype: PU_DTYPE_F16, PU_DTYPE_BF16 or PU_DTYPE_FP8_E4M3; the stored
+ *   values times k_scale / v_scale are the keys / values (per-tensor
+ *   scales; pass 1 for f16/bf16).
+ *   o bf16 [B,H,1,D]; lse fp32 [B,H] or NULL; workspace as pu_decode
+ *   (pu_decode_workspace_size(B, H, n, D)).
+ */
+PU_API int pu_decode_gqa(const void* q, int q_dtype,
+                         const void* k_cache, const void* v_cache, int kv_dtype,
+                         const int32_t* kv_lens, void* o, float* lse,
+                         void* workspace, size_t workspace_bytes,
+                         int64_t B, int64_t H, int64_t H_kv, int64_t n, int64_t D,
+                         float sm_scale, float k_scale, float v_scale, void* stream);
 
 /*
  * Allocation-free single-GPU decode step.  No counterpart in the reference:

@@ -227,14 +227,17 @@ def pipeline_emulation(q, k, v, *, causal: bool = False, scale: float | None = N
 
 def decode_forward(q, k_cache, v_cache, *, kv_lens=None, scale: float | None = None,
                    dtype=np.float64):
-    """One query token per (b, h).  q [B,H,1,D], caches [B,H,N,D]; returns (o [B,H,1,D], lse [B,H]).
+    """One query token per (b, h).  q [B,H,1,D], caches [B,H_kv,N,D]; returns (o [B,H,1,D], lse [B,H]).
 
     inference_decode.py:32-44 (softmax(q K^T / sqrt(D)) V) with the
-    length mask of decoding.py:42-44 when kv_lens is given.
+    length mask of decoding.py:42-44 when kv_lens is given.  With
+    H_kv < H (grouped heads, no reference counterpart) query head h reads
+    K/V head h // (H // H_kv).
     """
     q = np.asarray(q, dtype=np.float32)
     B, H, _, D = q.shape
     N = k_cache.shape[2]
+    G = H // k_cache.shape[1]
     if scale is None:
         scale = 1.0 / np.sqrt(D)
     o = np.zeros((B, H, 1, D), dtype=dtype)
@@ -244,8 +247,8 @@ def decode_forward(q, k_cache, v_cache, *, kv_lens=None, scale: float | None = N
         if n <= 0:
             continue
         for h in range(H):
-            kh = np.asarray(k_cache[b, h, :n], dtype=np.float32).astype(dtype)
-            vh = np.asarray(v_cache[b, h, :n], dtype=np.float32).astype(dtype)
+            kh = np.asarray(k_cache[b, h // G, :n], dtype=np.float32).astype(dtype)
+            vh = np.asarray(v_cache[b, h // G, :n], dtype=np.float32).astype(dtype)
             s = (kh @ q[b, h, 0].astype(dtype)) * dtype(scale)
             m = s.max()
             p = np.exp(s - m)

@@ -18,6 +18,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "pu_host.cuh"
 #include "pu_ptx.cuh"
@@ -27,7 +28,6 @@ namespace decode {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 8;        // rows in flight per lane group per iteration
 constexpr int kCtasPerSm = 2;     // occupancy the launch bounds ask for
 constexpr int kWaves = 4;         // CTAs per SM slot the split heuristic aims at
 constexpr int kMinChunk = 256;    // fewest tokens one CTA is given
@@ -42,7 +42,9 @@ struct Params {
   const int32_t* lens;   // [B] global lengths or nullptr
   long long kv_offset;   // global position of local token 0
   int n_local;           // tokens in this shard's cache
-  int H;
+  int H;                 // query heads
+  int group = 1;         // query heads per K/V head (GQA / MQA); K/V head = h / group
+  float o_scale = 1.f;   // factor on every output record (the fp8 V scale)
   int splits;            // CTAs per (b, h)
   int chunk;             // tokens per CTA (multiple of 16)
   float scale_log2;      // sm_scale * log2(e)
@@ -113,6 +115,51 @@ __device__ __forceinline__ uint4 ld_stream_if(const uint4* p, bool pred) {
       : "l"(p), "r"((int)pred));
   return r;
 }
+
+// ld_stream_if for 8-byte rows pieces (fp8 caches: 8 elements per lane).
+__device__ __forceinline__ uint2 ld_stream_if(const uint2* p, bool pred) {
+  uint2 r = make_uint2(0, 0);
+  asm volatile(
+      "{\n .reg .pred q;\n setp.ne.b32 q, %3, 0;\n"
+      " @q ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];\n}"
+      : "+r"(r.x), "+r"(r.y)
+      : "l"(p), "r"((int)pred));
+  return r;
+}
+
+// Cache element types: the load word of 8 elements and its unpacking.
+template <typename T>
+struct KVIO {
+  using W = uint4;
+  static constexpr int kUnroll = 8;   // rows in flight per lane group
+  __device__ __forceinline__ static W ld(const T* p, bool pred) {
+    return ld_stream_if(reinterpret_cast<const uint4*>(p), pred);
+  }
+  __device__ __forceinline__ static void unpack(const W& w, float (&f)[8]) { unpack8<T>(w, f); }
+};
+
+// fp8 e4m3: 8 bytes per lane, twice the rows in flight for the same bytes
+template <>
+struct KVIO<__nv_fp8_e4m3> {
+  using W = uint2;
+  static constexpr int kUnroll = 16;
+  __device__ __forceinline__ static W ld(const __nv_fp8_e4m3* p, bool pred) {
+    return ld_stream_if(reinterpret_cast<const uint2*>(p), pred);
+  }
+  __device__ __forceinline__ static void unpack(const W& w, float (&f)[8]) {
+    const uint32_t u[2] = {w.x, w.y};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const __half2 lo(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(u[i] & 0xFFFFu), __NV_E4M3));
+      const __half2 hi(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(u[i] >> 16), __NV_E4M3));
+      const float2 a = __half22float2(lo), b = __half22float2(hi);
+      f[4 * i] = a.x;
+      f[4 * i + 1] = a.y;
+      f[4 * i + 2] = b.x;
+      f[4 * i + 3] = b.y;
+    }
+  }
+};
 
 // Merge (m, l, o[D]) records with a stable LogSumExp; m in log2 units.
 // Thread `d` (< D) produces column d.  Returns M and L through refs.
@@ -207,6 +254,8 @@ __global__ void __launch_bounds__(D) peer_combine_kernel(const unsigned long lon
 // every peer's exchange buffer when kPush).
 template <typename QT, typename KVT, int D, bool kFinal, bool kPaged, bool kPush = false>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Params p) {
+  using IO = KVIO<KVT>;
+  constexpr int kUnroll = IO::kUnroll;
   constexpr int LPR = D / 8;        // lanes per cache row
   constexpr int RPW = 32 / LPR;     // rows per warp instruction
   constexpr int ROWS_PER_ITER = kWarps * RPW * kUnroll;
@@ -244,8 +293,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
     for (int i = 0; i < 8; ++i) qf[i] *= p.scale_log2;
   }
 
-  const KVT* kb = static_cast<const KVT*>(p.k) + (size_t)bh * p.n_local * D + sub * 8;
-  const KVT* vb = static_cast<const KVT*>(p.v) + (size_t)bh * p.n_local * D + sub * 8;
+  // K/V head of this query head (GQA / MQA: `group` query heads share one)
+  const int h = bh % p.H;
+  const int h_kv = h / p.group;
+  const int H_kv = p.H / p.group;
+  const size_t kv_head = (size_t)b * H_kv + h_kv;
+  const KVT* kb = static_cast<const KVT*>(p.k) + kv_head * p.n_local * D + sub * 8;
+  const KVT* vb = static_cast<const KVT*>(p.v) + kv_head * p.n_local * D + sub * 8;
   // paged cache: token t of sequence b is row t % page_size of page
   // page_table[b][t / page_size]; out-of-range page numbers are reported
   // and their tokens skipped.  A warp's tokens of one iteration are TW
@@ -253,7 +307,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
   // the page size), so when page_size >= TW they share one page: its entry
   // is read once, one iteration ahead of its use.
   constexpr int TW = RPW * kUnroll;
-  const int h = bh % p.H;
   const int32_t* table_b = nullptr;
   bool one_page = false;
   int pg_next = 0;
@@ -267,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
   }
   const int page_mask = (1 << p.page_shift) - 1;
   auto page_row = [&](int pg, int t) -> size_t {
-    return ((((size_t)pg * p.H + h) << p.page_shift) + (t & page_mask)) * D;
+    return ((((size_t)pg * H_kv + h_kv) << p.page_shift) + (t & page_mask)) * D;
   };
 
   float m = -INFINITY, l = 0.f;
@@ -276,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
   for (int i = 0; i < 8; ++i) o[i] = 0.f;
 
   for (int base = t_begin + warp * TW; base < t_end; base += ROWS_PER_ITER) {
-    uint4 kw[kUnroll], vw[kUnroll];
+    typename IO::W kw[kUnroll], vw[kUnroll];
     bool tok_ok[kUnroll];
     if constexpr (kPaged) {
       if (one_page) {
@@ -290,8 +343,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
         for (int u = 0; u < kUnroll; ++u) {
           tok_ok[u] = page_ok && (base + u * RPW + rw < t_end);
           const size_t off = row0 + (size_t)(u * RPW + rw) * D;
-          kw[u] = ld_stream_if(reinterpret_cast<const uint4*>(kb + off), tok_ok[u]);
-          vw[u] = ld_stream_if(reinterpret_cast<const uint4*>(vb + off), tok_ok[u]);
+          kw[u] = IO::ld(kb + off, tok_ok[u]);
+          vw[u] = IO::ld(vb + off, tok_ok[u]);
         }
       } else {
 #pragma unroll
@@ -302,8 +355,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
           tok_ok[u] = (unsigned)pg < (unsigned)p.num_pages;
           if (t < t_end && !tok_ok[u]) record_device_error(PU_ERR_INVALID_ARGUMENT, kSiteDecodePage);
           const size_t off = tok_ok[u] ? page_row(pg, t) : 0;
-          kw[u] = ld_stream_if(reinterpret_cast<const uint4*>(kb + off), tok_ok[u]);
-          vw[u] = ld_stream_if(reinterpret_cast<const uint4*>(vb + off), tok_ok[u]);
+          kw[u] = IO::ld(kb + off, tok_ok[u]);
+          vw[u] = IO::ld(vb + off, tok_ok[u]);
         }
       }
     } else {
@@ -311,15 +364,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
       for (int u = 0; u < kUnroll; ++u) {
         const int t = base + u * RPW + rw;
         tok_ok[u] = t < t_end;
-        kw[u] = ld_stream_if(reinterpret_cast<const uint4*>(kb + (size_t)t * D), tok_ok[u]);
-        vw[u] = ld_stream_if(reinterpret_cast<const uint4*>(vb + (size_t)t * D), tok_ok[u]);
+        kw[u] = IO::ld(kb + (size_t)t * D, tok_ok[u]);
+        vw[u] = IO::ld(vb + (size_t)t * D, tok_ok[u]);
       }
     }
     float s[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       float kf[8];
-      unpack8<KVT>(kw[u], kf);
+      IO::unpack(kw[u], kf);
       float acc = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc = fmaf(qf[i], kf[i], acc);
@@ -347,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
       const float pu_ = ex2(s[u] - m_new);
       l += pu_;
       float vf[8];
-      unpack8<KVT>(vw[u], vf);
+      IO::unpack(vw[u], vf);
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = fmaf(pu_, vf[i], o[i]);
     }
@@ -378,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
         O += w * sm_o[g][tid];
       }
     }
-    rec[2 + tid] = O;
+    rec[2 + tid] = O * p.o_scale;
     if (tid == 0) {
       rec[0] = M;
       rec[1] = L;
@@ -502,30 +555,37 @@ inline size_t workspace_bytes_any(long long BH, long long n_local, long long D, 
                   make_plan(BH, n_local, D, num_sms, true).total_bytes);
 }
 
-template <bool kFinal, bool kPaged = false, bool kPush = false>
-int launch(const Params& prm, int q_dtype, int kv_dtype, int D, int BH, cudaStream_t st) {
-  dim3 grid(prm.splits, BH);
-  dim3 block(kThreads);
-#define PU_DECODE_LAUNCH(QT, KVT, DD) split_kv_kernel<QT, KVT, DD, kFinal, kPaged, kPush><<<grid, block, 0, st>>>(prm)
-  const bool qh = (q_dtype == PU_DTYPE_F16);
-  const bool kh = (kv_dtype == PU_DTYPE_F16);
-  if (D == 128) {
-    if (qh && kh) PU_DECODE_LAUNCH(__half, __half, 128);
-    else if (qh && !kh) PU_DECODE_LAUNCH(__half, __nv_bfloat16, 128);
-    else if (!qh && kh) PU_DECODE_LAUNCH(__nv_bfloat16, __half, 128);
-    else PU_DECODE_LAUNCH(__nv_bfloat16, __nv_bfloat16, 128);
+template <bool kFinal, bool kPaged, bool kPush, typename QT, int DD>
+int launch_kv(const Params& prm, int kv_dtype, dim3 grid, cudaStream_t st) {
+  if (kv_dtype == PU_DTYPE_F16) {
+    split_kv_kernel<QT, __half, DD, kFinal, kPaged, kPush><<<grid, kThreads, 0, st>>>(prm);
+  } else if (kv_dtype == PU_DTYPE_BF16) {
+    split_kv_kernel<QT, __nv_bfloat16, DD, kFinal, kPaged, kPush><<<grid, kThreads, 0, st>>>(prm);
   } else {
-    if (qh && kh) PU_DECODE_LAUNCH(__half, __half, 64);
-    else if (qh && !kh) PU_DECODE_LAUNCH(__half, __nv_bfloat16, 64);
-    else if (!qh && kh) PU_DECODE_LAUNCH(__nv_bfloat16, __half, 64);
-    else PU_DECODE_LAUNCH(__nv_bfloat16, __nv_bfloat16, 64);
+    // fp8 caches are read by the single-GPU final-output step
+    if constexpr (kFinal && !kPaged && !kPush) {
+      split_kv_kernel<QT, __nv_fp8_e4m3, DD, kFinal, kPaged, kPush><<<grid, kThreads, 0, st>>>(prm);
+    } else {
+      return set_error(PU_ERR_UNSUPPORTED, "fp8 caches: single-GPU dense decode only");
+    }
   }
-#undef PU_DECODE_LAUNCH
   return check_cuda(cudaGetLastError(), "split-KV decode launch");
 }
 
+template <bool kFinal, bool kPaged = false, bool kPush = false>
+int launch(const Params& prm, int q_dtype, int kv_dtype, int D, int BH, cudaStream_t st) {
+  const dim3 grid(prm.splits, BH);
+  const bool qh = (q_dtype == PU_DTYPE_F16);
+  if (D == 128)
+    return qh ? launch_kv<kFinal, kPaged, kPush, __half, 128>(prm, kv_dtype, grid, st)
+              : launch_kv<kFinal, kPaged, kPush, __nv_bfloat16, 128>(prm, kv_dtype, grid, st);
+  return qh ? launch_kv<kFinal, kPaged, kPush, __half, 64>(prm, kv_dtype, grid, st)
+            : launch_kv<kFinal, kPaged, kPush, __nv_bfloat16, 64>(prm, kv_dtype, grid, st);
+}
+
 inline int check_args(const void* q, int q_dtype, const void* k, const void* v, int kv_dtype,
-                      long long B, long long H, long long n, long long D) {
+                      long long B, long long H, long long n, long long D, bool allow_fp8 = false) {
+  if (allow_fp8 && kv_dtype == PU_DTYPE_FP8_E4M3) kv_dtype = PU_DTYPE_F16;  // same checks otherwise
   if (!q || !k || !v) return set_error(PU_ERR_INVALID_ARGUMENT, "null q/k/v pointer");
   if (B <= 0 || H <= 0 || n <= 0) return set_error(PU_ERR_INVALID_ARGUMENT, "B, H and the cache length must be positive");
   if (D != 128 && D != 64) return set_error(PU_ERR_UNSUPPORTED, "decode head size %lld (supported: 64, 128)", D);
@@ -621,6 +681,43 @@ int pu_decode_combine(const float* partials, int64_t G, void* o, float* lse, int
   else
     combine_kernel<64><<<BH, 64, 0, st>>>(partials, (int)G, BH, static_cast<__nv_bfloat16*>(o), lse);
   return pu::check_cuda(cudaGetLastError(), "decode combine launch");
+}
+
+int pu_decode_gqa(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
+                  const int32_t* kv_lens, void* o, float* lse, void* workspace, size_t workspace_bytes,
+                  int64_t B, int64_t H, int64_t H_kv, int64_t n, int64_t D, float sm_scale, float k_scale,
+                  float v_scale, void* stream) {
+  using namespace pu::decode;
+  int rc = check_args(q, q_dtype, k_cache, v_cache, kv_dtype, B, H, n, D, true);
+  if (rc) return rc;
+  if (!o) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null output");
+  if (H_kv <= 0 || H % H_kv != 0)
+    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "H = %lld is not a multiple of H_kv = %lld", (long long)H,
+                         (long long)H_kv);
+  if (!(k_scale > 0.f) || !(v_scale > 0.f) || !isfinite(k_scale) || !isfinite(v_scale))
+    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "k_scale and v_scale must be positive and finite");
+  const Plan pl = make_plan(B * H, n, D, pu::sm_count(), kv_lens != nullptr);
+  if (!workspace || workspace_bytes < pl.total_bytes)
+    return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
+                         workspace_bytes);
+  Params prm{};
+  prm.q = q;
+  prm.k = k_cache;
+  prm.v = v_cache;
+  prm.lens = kv_lens;
+  prm.kv_offset = 0;
+  prm.n_local = (int)n;
+  prm.H = (int)H;
+  prm.group = (int)(H / H_kv);
+  prm.o_scale = v_scale;
+  prm.splits = pl.splits;
+  prm.chunk = pl.chunk;
+  prm.scale_log2 = sm_scale * k_scale * kLog2e;
+  prm.ws_rec = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.rec_off);
+  prm.ws_count = static_cast<int*>(workspace);
+  prm.o = static_cast<__nv_bfloat16*>(o);
+  prm.lse = lse;
+  return launch<true>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -21,6 +21,7 @@ PU_ERR_DEVICE_TIMEOUT = 5
 PU_DTYPE_BF16 = 0
 PU_DTYPE_F16 = 1
 PU_DTYPE_F32 = 2
+PU_DTYPE_FP8_E4M3 = 3
 
 _LIB_PATH = Path(__file__).resolve().parent / "_native" / "libpu_attn.so"
 
@@ -54,6 +55,9 @@ SIGNATURES = {
     "pu_decode_noalloc": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p,
                                  _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _float,
                                  _c_void_p]),
+    "pu_decode_gqa": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p,
+                             _c_void_p, _c_void_p, _size_t, _i64, _i64, _i64, _i64, _i64, _float,
+                             _float, _float, _c_void_p]),
     "pu_decode_paged_workspace_size": (_size_t, [_i64, _i64, _i64, _i64, _i64]),
     "pu_decode_paged": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _i64,
                                _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _size_t,

@@ -24,6 +24,8 @@ Keyword-only additions:
               "peer" (partials stored straight into every rank's exchange
               buffer over NVLink, flags instead of a collective; see
               distributed/peer.py)
+  k_scale, v_scale  per-tensor scales of an fp8 (torch.float8_e4m3fn) cache:
+              keys / values are the stored values times the scale
   page_table  int32 [B, max_pages_per_seq]: the caches are then page pools
               [num_pages, H, page_size, D] (see kernels/paged.py) and
               kv_lens is required; single GPU only.
@@ -41,6 +43,8 @@ from .. import _lib
 __all__ = ["pallas_flash_decoding", "decode_partial", "decode_combine", "DecodeWorkspace"]
 
 _DT = {torch.float16: _lib.PU_DTYPE_F16, torch.bfloat16: _lib.PU_DTYPE_BF16}
+_FP8 = getattr(torch, "float8_e4m3fn", None)
+_DT_KV = {**_DT, **({_FP8: _lib.PU_DTYPE_FP8_E4M3} if _FP8 is not None else {})}
 
 
 class DecodeWorkspace:
@@ -63,9 +67,9 @@ class DecodeWorkspace:
             return buf
 
 
-def _prep(t: torch.Tensor, dev: torch.device) -> torch.Tensor:
+def _prep(t: torch.Tensor, dev: torch.device, kinds=_DT) -> torch.Tensor:
     t = t.to(dev, non_blocking=True)
-    if t.dtype not in _DT:
+    if t.dtype not in kinds:
         t = t.to(torch.bfloat16)
     return t.contiguous()
 
@@ -109,7 +113,8 @@ def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch
                           kv_lens: Optional[torch.Tensor] = None,
                           sm_scale: Optional[float] = None, return_lse: bool = False,
                           group=None, transport: str = "nccl",
-                          page_table: Optional[torch.Tensor] = None):
+                          page_table: Optional[torch.Tensor] = None,
+                          k_scale: float = 1.0, v_scale: float = 1.0):
     """One decode step of attention for a query token per (b, h)."""
     if page_table is not None:
         from .paged import paged_decode
@@ -119,12 +124,17 @@ def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch
                             return_lse=return_lse)
     if q.dim() != 4 or q.shape[2] != 1:
         raise ValueError("q must be [B, H, 1, D]")
-    if k_cache.shape != v_cache.shape or k_cache.shape[:2] != q.shape[:2] \
-            or k_cache.shape[3] != q.shape[3]:
+    if k_cache.shape != v_cache.shape or k_cache.shape[0] != q.shape[0] \
+            or k_cache.shape[3] != q.shape[3] or q.shape[1] % k_cache.shape[1] != 0:
         raise ValueError(f"cache shape {tuple(k_cache.shape)} does not match q {tuple(q.shape)}")
+    H_kv = k_cache.shape[1]
+    grouped = H_kv != q.shape[1] or k_cache.dtype == _FP8 or k_scale != 1.0 or v_scale != 1.0
+    if grouped and (group is not None or page_table is not None):
+        raise ValueError("grouped K/V heads and fp8 caches: single-GPU dense caches only")
     host = not q.is_cuda
     dev = torch.device("cuda", torch.cuda.current_device()) if host else q.device
-    q_, k_, v_ = _prep(q, dev), _prep(k_cache, dev), _prep(v_cache, dev)
+    kinds = _DT_KV if grouped else _DT
+    q_, k_, v_ = _prep(q, dev), _prep(k_cache, dev, kinds), _prep(v_cache, dev, kinds)
     B, H, _, D = q_.shape
     if D not in (64, 128):
         raise ValueError(f"decode head size {D} (supported: 64, 128)")
@@ -138,7 +148,17 @@ def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch
     lib = _lib.lib()
     stream = torch.cuda.current_stream().cuda_stream
     n_local = k_.shape[2]
-    if group is None:
+    if grouped:
+        o = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device=dev)
+        lse = torch.empty((B, H), dtype=torch.float32, device=dev)
+        ws = DecodeWorkspace.get(dev, int(lib.pu_decode_workspace_size(B, H, n_local, D)))
+        _lib.check(lib.pu_decode_gqa(q_.data_ptr(), _DT[q_.dtype], k_.data_ptr(), v_.data_ptr(),
+                                     _DT_KV[k_.dtype],
+                                     lens.data_ptr() if lens is not None else None,
+                                     o.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), B, H,
+                                     H_kv, n_local, D, float(sm_scale), float(k_scale),
+                                     float(v_scale), stream), "pu_decode_gqa")
+    elif group is None:
         o = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device=dev)
         lse = torch.empty((B, H), dtype=torch.float32, device=dev)
         need = int(lib.pu_decode_workspace_size(B, H, n_local, D))

@@ -201,3 +201,19 @@ def test_golden_decode():
     np.testing.assert_allclose(lse, g["lse"], atol=1e-5)
     co, cl = orc.lse_combine(g["partials"])
     np.testing.assert_allclose(co.reshape(o.shape), g["o"], atol=1e-5)
+
+
+def test_decode_grouped_heads_equal_repeated_cache():
+    """Grouped K/V heads (query head h reads K/V head h // G) give the same
+    result as a cache whose K/V heads are repeated G times."""
+    rng = np.random.Generator(np.random.PCG64(31))
+    B, H, H_kv, N, D = 2, 8, 2, 50, 16
+    q = rng.standard_normal((B, H, 1, D)).astype(np.float32)
+    k = rng.standard_normal((B, H_kv, N, D)).astype(np.float32)
+    v = rng.standard_normal((B, H_kv, N, D)).astype(np.float32)
+    lens = np.array([50, 7])
+    o1, l1 = orc.decode_forward(q, k, v, kv_lens=lens)
+    G = H // H_kv
+    o2, l2 = orc.decode_forward(q, np.repeat(k, G, axis=1), np.repeat(v, G, axis=1), kv_lens=lens)
+    np.testing.assert_array_equal(o1, o2)
+    np.testing.assert_array_equal(l1, l2)
