@@ -44,9 +44,11 @@ L2_BYTES = 126 * 1024 * 1024
 # DRAM bytes (read + write) per launch from one ncu capture of this workload
 # (see the summaries under profiles/); re-measured whenever a kernel changes.
 NCU_TRAFFIC_BYTES = {
-    "attn_fwd": 201_384_192 + 50_688_512,
-    "attn_bwd": (270_716_160 + 109_300_480) + (270_625_280 + 52_647_680) + 135_000_000,
-    "split_kv": 536_905_728 + 3_892_736,
+    "attn_fwd": 543_731_968 + 50_730_752,
+    # dK/dV + dQ measured; prep (reads O and dO, writes the row statistics) counted at
+    # its algorithmic 135 MB
+    "attn_bwd": (936_651_008 + 105_057_536) + (964_845_056 + 51_491_328) + 135_000_000,
+    "split_kv": 536_904_192 + 3_470_848,
 }
 
 
@@ -443,6 +445,37 @@ def bench_ragged_decode(steps: int, warmup: int, rank: int, world: int):
     return dense_us, paged_us, nbytes
 
 
+def bench_gqa_decode(steps: int, warmup: int):
+    """Grouped-head decode on one GPU: B=1, 32 query heads over 8 K/V heads,
+    32768 tokens, D=128, fp16 and fp8 (e4m3) caches.  Returns
+    {dtype: (us, K/V bytes read)}."""
+    import torch
+    from pallas_flash.kernels import decoding as dec
+
+    B, H, H_kv, N, D = 1, 32, 8, 32768, 128
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5000)
+    q = torch.randn((B, H, 1, D), device="cuda", generator=g).to(torch.float16)
+    k = torch.randn((B, H_kv, N, D), device="cuda", generator=g)
+    v = torch.randn((B, H_kv, N, D), device="cuda", generator=g)
+    flush = L2Flush()
+    stream = torch.cuda.current_stream()
+    out = {}
+    caches = {"f16": (k.half(), v.half(), 1.0, 1.0)}
+    fp8 = getattr(torch, "float8_e4m3fn", None)
+    if fp8 is not None:
+        caches["fp8_e4m3"] = ((k / 0.25).to(fp8), (v / 0.25).to(fp8), 0.25, 0.25)
+    for name, (kc, vc, ks, vs) in caches.items():
+        def step():
+            return dec.pallas_flash_decoding(q, kc, vc, k_scale=ks, v_scale=vs)
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        us = _timed(step, steps, flush, stream)
+        out[name] = (us, 2 * kc.numel() * kc.element_size())
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -450,6 +483,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["pu", "reference"], default="pu")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--profile-leg", choices=["attn", "decode"], default=None,
+                    help="run only this leg and print no JSON (small runs for ncu captures)")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
     peaks = load_peaks()
@@ -459,9 +494,16 @@ def main():
 
     import torch
     rank, world, local = dist_init()
+    if args.profile_leg == "decode":
+        us, _, _ = bench_decode(args.steps, warmup, rank, world, "peer")
+        print(f"decode leg: {us:.1f} us/step", flush=True)
+        return
     clocks = ClockSampler(local).start()
     total_ms, fwd_ms, bwd_ms = bench_attention(args.steps, warmup, rank, world, clocks)
     clk = clocks.stop()
+    if args.profile_leg == "attn":
+        print(f"attention leg: {total_ms / args.steps:.3f} ms/step", flush=True)
+        return
     ms_step = allreduce_max(total_ms / args.steps, world)
     value = STEP_FLOPS * world / (ms_step * 1e-3) / 1e12
     bwd_ms_max = allreduce_max(bwd_ms, world)
@@ -472,6 +514,7 @@ def main():
     nccl_us = bench_decode(dec_steps, warmup, rank, world, "nccl")[0] if world > 1 else None
     rag_us, rag_paged_us, rag_bytes = bench_ragged_decode(max(5, min(args.steps, 20)), warmup,
                                                           rank, world)
+    gqa = bench_gqa_decode(max(5, min(args.steps, 50)), warmup) if world == 1 else None
 
     if rank == 0:
         bwd_flops = FWD_FLOPS * 2.5
@@ -482,7 +525,8 @@ def main():
                 "peak_source": peaks["source"] + " bf16 burst",
                 "traffic": NCU_TRAFFIC_BYTES["attn_bwd"],
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, "
-                                  "profiles/attn_bwd_*_causal_B4H16N4096D128.md"}
+                                  "profiles/attn_bwd_*_causal_B4H16N4096D128.md; above the "
+                                  "algorithmic bytes because heavy-first order re-reads from DRAM"}
         fwd_ach = FWD_FLOPS / (fwd_ms_max * 1e-3) / 1e12
         cpu = None
         if world == 1:
@@ -542,6 +586,15 @@ def main():
                       "GB_s": round(rag_bytes / (rag_us * 1e-6) / 1e9, 1),
                       "frac": round(rag_bytes / (rag_us * 1e-6) / 1e9 / (hbm * world), 4)},
             "l2": "1 GiB buffer written, then another 256 MB read, before every step"}
+        if gqa:
+            line["decode_gqa"] = {
+                "workload": "grouped-head decode B=1 H=32 H_kv=8 N=32768 D=128, one GPU",
+                "l2": "1 GiB buffer written, then another 256 MB read, before every step"}
+            for name, (us, nbytes) in gqa.items():
+                line["decode_gqa"][name] = {
+                    "us_per_step": round(us, 2), "kv_bytes": nbytes,
+                    "GB_s": round(nbytes / (us * 1e-6) / 1e9, 1),
+                    "frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4)}
         if rag_paged_us is not None:
             line["decode_ragged"]["paged"] = {
                 "page_size": RAG_PAGE, "page_order": "shuffled",
