@@ -158,6 +158,23 @@ def barrier(world: int):
         dist.barrier()
 
 
+_ALIGN = {}
+
+
+def device_align(world: int):
+    """Align the ranks on the device before a timed multi-GPU step: a 1-element
+    NCCL all-reduce on the current stream completes on every GPU at nearly the
+    same moment, so the start events that follow it are not skewed by how long
+    each GPU's preceding (untimed) work took."""
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        t = _ALIGN.get("t")
+        if t is None:
+            t = _ALIGN["t"] = torch.zeros(1, device="cuda")
+        dist.all_reduce(t)
+
+
 # ---------------------------------------------------------------------------
 # CPU baselines (rank 0, N=1, bounded samples of the same workloads)
 # ---------------------------------------------------------------------------
@@ -328,6 +345,7 @@ def bench_decode(steps: int, warmup: int, rank: int, world: int, transport: str 
     for _ in range(steps):
         barrier(world)                              # ranks start each step together
         flusher()                                   # evict the cache shard from L2
+        device_align(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         step()
@@ -365,15 +383,16 @@ def ragged_lens():
 
 class L2Flush:
     """Evicts the L2 between timed decode steps: writes a 1 GiB buffer, then
-    reads another twice the L2 size, so the lines left behind are clean and no
-    write-back of the flush lands inside the next timed step.  The ~0.2 ms of
-    flush work also lets the host enqueue the step before the GPU reaches the
-    start event, so the events time the device work only."""
+    reads another 1 GiB buffer.  The read must be this large: after a 256 MB
+    read, dirty lines of the write were still in L2 and the timed step paid
+    their write-backs (+7 us on the 32k-token decode).  The ~0.3 ms of flush
+    work also lets the host enqueue the step before the GPU reaches the start
+    event, so the events time the device work only."""
 
     def __init__(self):
         import torch
         self.w = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
-        self.r = torch.ones(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+        self.r = torch.ones((1 << 30) // 4, dtype=torch.float32, device="cuda")
         self.acc = torch.zeros((), dtype=torch.float32, device="cuda")
 
     def __call__(self):
@@ -382,11 +401,12 @@ class L2Flush:
         torch.sum(self.r, dim=0, out=self.acc)
 
 
-def _timed(fn, steps, flush, stream):
+def _timed(fn, steps, flush, stream, world: int = 1):
     import torch
     times = []
     for _ in range(steps):
         flush()
+        device_align(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         fn()
@@ -428,7 +448,7 @@ def bench_ragged_decode(steps: int, warmup: int, rank: int, world: int):
         dense()
     torch.cuda.synchronize()
     barrier(world)
-    dense_us = allreduce_max(_timed(dense, steps, flush, stream), world)
+    dense_us = allreduce_max(_timed(dense, steps, flush, stream, world), world)
     paged_us = None
     if world == 1:
         cache = paged.PagedKVCache.from_dense(k, v, lens, page_size=RAG_PAGE, shuffle_seed=1)
@@ -574,7 +594,7 @@ def main():
                                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                     "frac": round(dec_bytes / (dec_kus * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
                                     "traffic": NCU_TRAFFIC_BYTES["split_kv"] if world == 1 else None},
-                       "l2": "1 GiB buffer written, then another 256 MB read, before every step"},
+                       "l2": "1 GiB buffer written, then another 1 GiB read, before every step"},
         }
         hbm = peaks["hbm_gbs"]
         line["decode_ragged"] = {
@@ -585,11 +605,11 @@ def main():
             "dense": {"us_per_step": round(rag_us, 2),
                       "GB_s": round(rag_bytes / (rag_us * 1e-6) / 1e9, 1),
                       "frac": round(rag_bytes / (rag_us * 1e-6) / 1e9 / (hbm * world), 4)},
-            "l2": "1 GiB buffer written, then another 256 MB read, before every step"}
+            "l2": "1 GiB buffer written, then another 1 GiB read, before every step"}
         if gqa:
             line["decode_gqa"] = {
                 "workload": "grouped-head decode B=1 H=32 H_kv=8 N=32768 D=128, one GPU",
-                "l2": "1 GiB buffer written, then another 256 MB read, before every step"}
+                "l2": "1 GiB buffer written, then another 1 GiB read, before every step"}
             for name, (us, nbytes) in gqa.items():
                 line["decode_gqa"][name] = {
                     "us_per_step": round(us, 2), "kv_bytes": nbytes,

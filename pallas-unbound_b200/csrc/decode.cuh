@@ -161,24 +161,65 @@ struct KVIO<__nv_fp8_e4m3> {
   }
 };
 
-// Merge (m, l, o[D]) records with a stable LogSumExp; m in log2 units.
-// Thread `d` (< D) produces column d.  Returns M and L through refs.
+// Merge the nrec split records {m (log2 units), l, o[D]} of one (b, h) with a
+// stable LogSumExp, using every thread of the block: the maximum and the
+// weights 2^(m_g - M) are computed one record per thread, then thread d < D
+// sums column d over the records in order, eight loads in flight (a loop that
+// waited for each record's load in turn would chain one L2 round trip per
+// record at the end of the kernel).  M and L reach every thread, O threads
+// d < D.  sm_w: kThreads floats, sm_red: kWarps floats of shared memory.
 template <int D>
-__device__ __forceinline__ void merge_records(const float* rec, int nrec, int stride, int d,
-                                              float& M, float& L, float& O) {
-  M = -INFINITY;
-  for (int g = 0; g < nrec; ++g) M = fmaxf(M, __ldcg(rec + (size_t)g * stride));
+__device__ __forceinline__ void block_merge(const float* rec, int nrec, float* sm_w, float* sm_red, float& M,
+                                            float& L, float& O) {
+  constexpr int stride = D + 2;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  float mx = -INFINITY;
+  for (int g = t; g < nrec; g += kThreads) mx = fmaxf(mx, __ldcg(rec + (size_t)g * stride));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) sm_red[warp] = mx;
+  __syncthreads();
+  M = sm_red[0];
+#pragma unroll
+  for (int w = 1; w < kWarps; ++w) M = fmaxf(M, sm_red[w]);
+  __syncthreads();
   L = 0.f;
   O = 0.f;
-  if (M == -INFINITY) return;
-  for (int g = 0; g < nrec; ++g) {
-    const float* r = rec + (size_t)g * stride;
-    const float mg = __ldcg(r);
-    if (mg == -INFINITY) continue;
-    const float w = ex2(mg - M);
-    L += w * __ldcg(r + 1);
-    O += w * __ldcg(r + 2 + d);
+  if (M == -INFINITY) return;  // every record empty (the same M in every thread)
+  float lsum = 0.f;
+  for (int c = 0; c < nrec; c += kThreads) {
+    const int g = c + t;
+    float w = 0.f;
+    if (g < nrec) {
+      const float* r = rec + (size_t)g * stride;
+      const float mg = __ldcg(r);
+      const float lg = __ldcg(r + 1);
+      w = (mg == -INFINITY) ? 0.f : ex2(mg - M);
+      lsum += w * lg;
+    }
+    sm_w[t] = w;
+    __syncthreads();
+    if (t < D) {
+      const int n = min(kThreads, nrec - c);
+      const float* base = rec + (size_t)c * stride + 2 + t;
+      int j = 0;
+      for (; j + 8 <= n; j += 8) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) x[u] = __ldcg(base + (size_t)(j + u) * stride);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) O = fmaf(sm_w[j + u], x[u], O);
+      }
+      for (; j < n; ++j) O = fmaf(sm_w[j], __ldcg(base + (size_t)j * stride), O);
+    }
+    __syncthreads();
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+  if (lane == 0) sm_red[warp] = lsum;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) L += sm_red[w];
 }
 
 // Push-mode merge for one (b, h): wait (bounded) until the words of every
@@ -187,9 +228,11 @@ __device__ __forceinline__ void merge_records(const float* rec, int nrec, int st
 // the block (d = thread index; threads d >= D only join the vote).  A wait
 // that runs out records PU_ERR_DEVICE_TIMEOUT (detail kSiteDecodePeer) and
 // the output is zeros.
-__device__ __forceinline__ bool ll_wait(const unsigned long long* w, unsigned epoch, uint64_t timeout_ns,
-                                        float& value) {
-  unsigned long long x = ld_volatile_u64(w);
+// Value of the 64-bit word at w once it carries `epoch`: x is a first read
+// of it (issued earlier, with the other words' reads in flight), re-read with
+// a bounded wait only while its epoch does not match.
+__device__ __forceinline__ bool ll_settle(const unsigned long long* w, unsigned long long x, unsigned epoch,
+                                          uint64_t timeout_ns, float& value) {
   if ((unsigned)(x >> 32) != epoch) {
     const uint64_t t0 = global_timer_ns();
     do {
@@ -206,6 +249,18 @@ __device__ __forceinline__ void peer_merge(const unsigned long long* exch, int G
                                            uint64_t timeout_ns, __nv_bfloat16* o, float* lse, int d) {
   const unsigned long long* base = exch + (size_t)(epoch & 1u) * G * BH * (D + 2);
   float mg[kMaxPeers], lg[kMaxPeers], og[kMaxPeers];
+  unsigned long long wm[kMaxPeers], wl[kMaxPeers], wo[kMaxPeers];
+  // first reads of every rank's words, all in flight together
+#pragma unroll
+  for (int g = 0; g < kMaxPeers; ++g) {
+    wm[g] = wl[g] = wo[g] = 0ull;
+    if (d < D && g < G) {
+      const unsigned long long* r = base + ((size_t)g * BH + bh) * (D + 2);
+      wm[g] = ld_volatile_u64(r);
+      wl[g] = ld_volatile_u64(r + 1);
+      wo[g] = ld_volatile_u64(r + 2 + d);
+    }
+  }
   bool ok = true;
 #pragma unroll
   for (int g = 0; g < kMaxPeers; ++g) {
@@ -214,8 +269,8 @@ __device__ __forceinline__ void peer_merge(const unsigned long long* exch, int G
     og[g] = 0.f;
     if (d < D && g < G && ok) {
       const unsigned long long* r = base + ((size_t)g * BH + bh) * (D + 2);
-      ok = ll_wait(r, epoch, timeout_ns, mg[g]) && ll_wait(r + 1, epoch, timeout_ns, lg[g]) &&
-           ll_wait(r + 2 + d, epoch, timeout_ns, og[g]);
+      ok = ll_settle(r, wm[g], epoch, timeout_ns, mg[g]) && ll_settle(r + 1, wl[g], epoch, timeout_ns, lg[g]) &&
+           ll_settle(r + 2 + d, wo[g], epoch, timeout_ns, og[g]);
     }
   }
   if (!__syncthreads_and(ok)) {
@@ -265,6 +320,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
   __shared__ float sm_m[NGROUP];
   __shared__ float sm_l[NGROUP];
   __shared__ float sm_o[NGROUP][D];
+  __shared__ float sm_w[kThreads];
+  __shared__ float sm_red[kWarps];
   __shared__ int sm_last;
 
   const int tid = threadIdx.x;
@@ -448,9 +505,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
   __threadfence();
 
   // last CTA of this (b, h): merge every split record
+  float M, L, O;
+  block_merge<D>(p.ws_rec + (size_t)bh * p.splits * (D + 2), p.splits, sm_w, sm_red, M, L, O);
   if (tid < D) {
-    float M, L, O;
-    merge_records<D>(p.ws_rec + (size_t)bh * p.splits * (D + 2), p.splits, D + 2, tid, M, L, O);
     if constexpr (kFinal) {
       const float out = (L > 0.f) ? O / L : 0.f;
       p.o[(size_t)bh * D + tid] = __float2bfloat16_rn(out);
