@@ -465,6 +465,64 @@ def bench_ragged_decode(steps: int, warmup: int, rank: int, world: int):
     return dense_us, paged_us, nbytes
 
 
+OP_T, OP_K, OP_N = 4 * 4096, 16 * 128, 2048
+
+
+def bench_outproj(steps: int, warmup: int, rank: int, world: int):
+    """Attention output projection + TP all-reduce: every rank multiplies its
+    16 heads' output [16384, 2048] by its rows of W_O [2048, 2048]; the
+    partial products are summed over the ranks (weak scaling: K per rank is
+    fixed).  Returns {transport: us} (max over ranks)."""
+    import torch
+    from pallas_flash.distributed.outproj import out_proj_all_reduce
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(6000 + rank)
+    o = torch.randn((OP_T, OP_K), device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn((OP_K, OP_N), device="cuda", generator=g) / OP_K ** 0.5).to(torch.bfloat16)
+    y = torch.empty((OP_T, OP_N), device="cuda", dtype=torch.bfloat16)
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        group = dist.group.WORLD
+    else:
+        import torch.distributed as dist
+        if not dist.is_initialized():
+            dist.init_process_group("gloo", init_method="tcp://127.0.0.1:" + str(_free_port()),
+                                    rank=0, world_size=1)
+        group = dist.group.WORLD
+    stream = torch.cuda.current_stream()
+    out = {}
+    for transport in ("peer", "nccl"):
+        if world == 1 and transport == "nccl":
+            fn = lambda: torch.matmul(o, w, out=y)
+        else:
+            fn = lambda: out_proj_all_reduce(o, w, group, transport=transport, out=y)
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        times = []
+        for _ in range(steps):
+            barrier(world)
+            device_align(world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        out[transport] = allreduce_max(statistics.median(times) * 1e3, world)
+    return out
+
+
+def _free_port() -> int:
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def bench_gqa_decode(steps: int, warmup: int):
     """Grouped-head decode on one GPU: B=1, 32 query heads over 8 K/V heads,
     32768 tokens, D=128, fp16 and fp8 (e4m3) caches.  Returns
@@ -535,6 +593,7 @@ def main():
     rag_us, rag_paged_us, rag_bytes = bench_ragged_decode(max(5, min(args.steps, 20)), warmup,
                                                           rank, world)
     gqa = bench_gqa_decode(max(5, min(args.steps, 50)), warmup) if world == 1 else None
+    op = bench_outproj(max(5, min(args.steps, 20)), warmup, rank, world)
 
     if rank == 0:
         bwd_flops = FWD_FLOPS * 2.5
@@ -606,6 +665,21 @@ def main():
                       "GB_s": round(rag_bytes / (rag_us * 1e-6) / 1e9, 1),
                       "frac": round(rag_bytes / (rag_us * 1e-6) / 1e9 / (hbm * world), 4)},
             "l2": "1 GiB buffer written, then another 1 GiB read, before every step"}
+        op_flops = 2 * OP_T * OP_K * OP_N
+        link_bytes = 2 * (world - 1) * OP_T * OP_N * 2 // world   # partials out + results out, per rank
+        op_floor_us = max(op_flops / (peaks["bf16_tflops"] * 1e12), link_bytes / 770e9) * 1e6
+        line["outproj"] = {
+            "workload": f"out-projection + TP all-reduce: per rank [{OP_T}, {OP_K}] x [{OP_K}, {OP_N}] bf16, "
+                        f"partials summed over {world} GPU(s), result on every rank",
+            "fused_peer_us": round(op["peer"], 2),
+            ("matmul_nccl_allreduce_us" if world > 1 else "cublas_matmul_us"): round(op["nccl"], 2),
+            "gemm_TFLOP_s_per_gpu": round(op_flops / (op["peer"] * 1e-6) / 1e12, 1),
+            "nvlink_bytes_out_per_gpu": link_bytes,
+            "roofline": {"bound": "tensor" if world == 1 else "max(tensor, nvlink)",
+                         "floor_us": round(op_floor_us, 2),
+                         "frac": round(op_floor_us / op["peer"], 4),
+                         "peaks": f"{peaks['bf16_tflops']} TFLOP/s bf16 (measured), 770 GB/s NVLink per "
+                                  "direction (measured peer copy)"}}
         if gqa:
             line["decode_gqa"] = {
                 "workload": "grouped-head decode B=1 H=32 H_kv=8 N=32768 D=128, one GPU",
@@ -632,6 +706,12 @@ def main():
         peer.close_all()
         dist.barrier()
         dist.destroy_process_group()
+    else:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            from pallas_flash.distributed import peer
+            peer.close_all()
+            dist.destroy_process_group()
 
 
 def run_reference(args, warmup):

@@ -338,6 +338,33 @@ PU_API int pu_decode_sharded(const void* q, int q_dtype,
                              int64_t B, int64_t H, int64_t n_local, int64_t D,
                              float sm_scale, uint64_t timeout_ns, void* stream);
 
+/*
+ * Attention output projection fused with the tensor-parallel all-reduce.
+ * Replaces the partial out-projection + all_reduce_tp (psum over the 'tp'
+ * axis) of src/pallas_flash/distributed/collectives.py:27-41, the step after
+ * attention when heads are sharded over devices.
+ *
+ * G ranks (one process per GPU, G <= 8, peer access between the GPUs) each
+ * hold o_local [T, K] (this rank's heads' attention output) and w_local
+ * [K, N] (the matching rows of W_O), bf16 row-major; every rank receives
+ * y = sum_g o_g w_g [T, N] bf16 (identical on all ranks).  T must be a
+ * multiple of 128, N of 256, K of 64.  The exchange buffers are set up as
+ * for pu_decode_push (pu_peer_alloc / pu_peer_open) with
+ * pu_outproj_exchange_bytes(T, N, G) bytes each; exchange[g] = this
+ * process's pointer to rank g's buffer.  All ranks call with the same epoch
+ * (1, 2, 3, ... in lockstep).  One tcgen05 GEMM kernel stores each bf16
+ * partial tile into its owner's buffer over NVLink, the owners reduce and
+ * broadcast, and every rank copies the result into y; each wait is bounded
+ * by timeout_ns (<= 2 s): on expiry pu_device_status reports
+ * PU_ERR_DEVICE_TIMEOUT, detail 401.
+ */
+PU_API size_t pu_outproj_exchange_bytes(int64_t T, int64_t N, int64_t G);
+
+PU_API int pu_outproj_allreduce(const void* o_local, const void* w_local, void* y,
+                                void* const* exchange, int64_t G, int64_t rank, uint32_t epoch,
+                                int64_t T, int64_t K, int64_t N, uint64_t timeout_ns,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

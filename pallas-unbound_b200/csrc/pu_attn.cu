@@ -5,6 +5,7 @@
 #include "decode.cuh"
 #include "paged.cuh"
 #include "peer.cuh"
+#include "outproj.cuh"
 #include "attn_fwd.cuh"
 #include "attn_bwd.cuh"
 

@@ -76,6 +76,9 @@ SIGNATURES = {
                                  _c_void_p, _i64, _i64, ctypes.c_uint32, _c_void_p, _c_void_p,
                                  _c_void_p, _size_t, _i64, _i64, _i64, _i64, _float,
                                  ctypes.c_uint64, _c_void_p]),
+    "pu_outproj_exchange_bytes": (_size_t, [_i64, _i64, _i64]),
+    "pu_outproj_allreduce": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
+                                    ctypes.c_uint32, _i64, _i64, _i64, ctypes.c_uint64, _c_void_p]),
     "pu_kv_append": (_int, [_c_void_p, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p, _i64,
                             _i64, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p]),
 }

@@ -25,24 +25,25 @@ import torch.distributed as dist
 
 from .. import _lib
 
-__all__ = ["PeerExchange", "get_exchange"]
+__all__ = ["PeerBuffers", "PeerExchange", "get_exchange", "get_cached", "close_all"]
 
 IPC_HANDLE_BYTES = 64
 DEFAULT_TIMEOUT_NS = 1_000_000_000  # 1 s
 
 
-class PeerExchange:
-    """Exchange buffers of one process group for one (B, H, D) decode shape."""
+class PeerBuffers:
+    """One zeroed, IPC-exportable device buffer per rank of `group`, mapped
+    into every rank's address space (pu_peer_alloc / pu_peer_open).
+    `ptrs[g]` is this process's pointer to rank g's buffer.  Collective."""
 
-    def __init__(self, B: int, H: int, D: int, group=None):
+    def __init__(self, nbytes: int, group=None):
         self.group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
         if not 1 <= self.world <= 8:
-            raise ValueError("peer exchange supports 1..8 ranks")
-        self.B, self.H, self.D = B, H, D
+            raise ValueError("peer buffers support 1..8 ranks")
         lib = _lib.lib()
-        self.nbytes = int(lib.pu_decode_exchange_bytes(B, H, D, self.world))
+        self.nbytes = int(nbytes)
         local = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
         _lib.check(lib.pu_peer_alloc(self.nbytes, ctypes.byref(local), handle), "pu_peer_alloc")
@@ -66,8 +67,38 @@ class PeerExchange:
             raise
         self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         self.epoch = 0
-        # every rank has mapped every buffer before anyone pushes
+        # every rank has mapped every buffer before anyone stores into it
         dist.barrier(group=self.group)
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        if self.epoch >= 2 ** 31:
+            raise RuntimeError("epoch counter exhausted; create new buffers")
+        return self.epoch
+
+    def _release(self):
+        lib = _lib.lib()
+        for p in self._opened:
+            lib.pu_peer_close(p)
+        self._opened = []
+        if self._local:
+            lib.pu_peer_free(self._local)
+            self._local = None
+
+    def close(self):
+        """Collective: unmap and free once no rank can still store."""
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self._release()
+
+
+class PeerExchange(PeerBuffers):
+    """Exchange buffers of one process group for one (B, H, D) decode shape."""
+
+    def __init__(self, B: int, H: int, D: int, group=None):
+        g = group if group is not None else dist.group.WORLD
+        self.B, self.H, self.D = B, H, D
+        super().__init__(int(_lib.lib().pu_decode_exchange_bytes(B, H, D, dist.get_world_size(g))), g)
 
     def decode(self, q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor, *,
                kv_offset: int, kv_lens: Optional[torch.Tensor], sm_scale: float,
@@ -77,9 +108,7 @@ class PeerExchange:
         B, H, D = self.B, self.H, self.D
         lib = _lib.lib()
         stream = torch.cuda.current_stream().cuda_stream
-        self.epoch += 1
-        if self.epoch >= 2 ** 31:
-            raise RuntimeError("epoch counter exhausted; create a new exchange")
+        self.next_epoch()
         n_local = k_shard.shape[2]
         o = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device=q.device)
         lse = torch.empty((B, H), dtype=torch.float32, device=q.device)
@@ -93,20 +122,6 @@ class PeerExchange:
                    "pu_decode_sharded")
         return o, lse
 
-    def _release(self):
-        lib = _lib.lib()
-        for p in self._opened:
-            lib.pu_peer_close(p)
-        self._opened = []
-        if self._local:
-            lib.pu_peer_free(self._local)
-            self._local = None
-
-    def close(self):
-        """Collective: unmap and free once no rank can still push."""
-        torch.cuda.synchronize()
-        dist.barrier(group=self.group)
-        self._release()
 
 
 _cache: dict = {}
@@ -115,11 +130,16 @@ _cache_lock = threading.Lock()
 
 def get_exchange(B: int, H: int, D: int, group=None) -> PeerExchange:
     """Cached PeerExchange per (group, device, B, H, D).  Collective on first use."""
-    key = (id(group), torch.cuda.current_device(), B, H, D)
+    return get_cached(("decode", B, H, D), lambda: PeerExchange(B, H, D, group), group)
+
+
+def get_cached(shape_key, make, group=None):
+    """Cached peer buffers per (group, device, shape_key).  Collective on first use."""
+    key = (id(group), torch.cuda.current_device()) + tuple(shape_key)
     with _cache_lock:
         ex = _cache.get(key)
     if ex is None:
-        ex = PeerExchange(B, H, D, group)
+        ex = make()
         with _cache_lock:
             _cache[key] = ex
     return ex

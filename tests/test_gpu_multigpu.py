@@ -9,6 +9,9 @@
   (both exchange slots), and a merge whose peers never publish runs out of
   its bounded wait, is reported (PU_ERR_DEVICE_TIMEOUT, detail 304), and
   leaves the context usable.
+* Output projection fused with the TP all-reduce (pu_outproj_allreduce):
+  every rank's result equals the fp32 sum of all ranks' products (bf16
+  tolerance) and is bitwise identical across ranks, over consecutive calls.
 * Head-partitioned training attention: each rank runs forward + backward
   on its heads only (no collective); the gathered outputs match the oracle.
 Runs world_size 2 as spawned processes with NCCL_NVLS_ENABLE=0.
@@ -90,6 +93,25 @@ def _worker(rank, world, port, out_dir):
     o_p, _ = pallas_flash_decoding(q.cuda(), ks, vs, kv_lens=lens.cuda(), group=dist.group.WORLD,
                                    transport="peer", return_lse=True)
     res["after_timeout"] = orc.compare(o_p.float().cpu().numpy(), ro)
+    # --- output projection + TP all-reduce over peer memory ---
+    from pallas_flash.distributed.outproj import out_proj_all_reduce
+    T, Kl, Nm = 1024, 256, 1024
+    worst = 0.0
+    for step in range(3):
+        os_ = [randn((T, Kl), 200 + 10 * step + g) for g in range(world)]
+        ws_ = [(randn((Kl, Nm), 300 + 10 * step + g).float() / Kl ** 0.5).to(torch.bfloat16)
+               for g in range(world)]
+        y = out_proj_all_reduce(os_[rank].cuda(), ws_[rank].cuda(), dist.group.WORLD)
+        ref = sum(os_[g].float() @ ws_[g].float() for g in range(world))
+        yc = y.float().cpu()
+        err = (yc - ref).abs().max().item() / ref.abs().max().item()
+        rel = ((yc - ref).norm() / ref.norm()).item()
+        worst = max(worst, err, rel)
+        ys = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(ys, y)
+        res["outproj_same"] = all(torch.equal(ys[0], t) for t in ys)
+    res["outproj_err"] = worst
+    res["outproj_status"] = list(_lib.device_status())
     peer.close_all()
     # --- head-partitioned training attention ---
     B, H, N, D = 1, 4, 512, 128
@@ -126,6 +148,7 @@ def test_two_gpu_decode_and_partitioned_training(tmp_path, built_lib):
         assert res["peer_equal"] and res["peer_status"] == [0, 0], res
         assert res["timeout_status"] == [5, 304], res
         assert res["after_timeout"]["max_abs"] <= 2e-2 and res["after_timeout"]["rel"] <= 1e-2, res
+        assert res["outproj_same"] and res["outproj_err"] <= 1e-2 and res["outproj_status"] == [0, 0], res
         assert res["tr_o"]["max_abs"] <= 2e-2 and res["tr_o"]["rel"] <= 1e-2, res
         for g in ("dq", "dk", "dv"):
             assert res["tr_" + g]["rel"] <= 3e-2, res
