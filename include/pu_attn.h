@@ -187,9 +187,15 @@ PU_API int pu_decode(const void* q, int q_dtype,
  *   kv_dtype: PU_DTYPE_F16, PU_DTYPE_BF16 or PU_DTYPE_FP8_E4M3; the stored
  *   values times k_scale / v_scale are the keys / values (per-tensor
  *   scales; pass 1 for f16/bf16).
- *   o bf16 [B,H,1,D]; lse fp32 [B,H] or NULL; workspace as pu_decode
- *   (pu_decode_workspace_size(B, H, n, D)).
+ *   With H / H_kv = 2, 4 or 8 one CTA serves all query heads of a K/V head,
+ *   so each K/V byte is read from DRAM once.
+ *   o bf16 [B,H,1,D]; lse fp32 [B,H] or NULL; workspace of
+ *   pu_decode_gqa_workspace_size(B, H, H_kv, n, D) bytes, zeroed before its
+ *   first use (left zeroed, as for pu_decode).
  */
+/* Bytes of workspace pu_decode_gqa needs (0 on invalid sizes). */
+PU_API size_t pu_decode_gqa_workspace_size(int64_t B, int64_t H, int64_t H_kv, int64_t n, int64_t D);
+
 PU_API int pu_decode_gqa(const void* q, int q_dtype,
                          const void* k_cache, const void* v_cache, int kv_dtype,
                          const int32_t* kv_lens, void* o, float* lse,

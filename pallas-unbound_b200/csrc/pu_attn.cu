@@ -4,6 +4,7 @@
 #include "capi.cuh"
 #include "decode.cuh"
 #include "paged.cuh"
+#include "gqa.cuh"
 #include "peer.cuh"
 #include "outproj.cuh"
 #include "attn_fwd.cuh"

@@ -55,6 +55,7 @@ SIGNATURES = {
     "pu_decode_noalloc": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p,
                                  _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _float,
                                  _c_void_p]),
+    "pu_decode_gqa_workspace_size": (_size_t, [_i64, _i64, _i64, _i64, _i64]),
     "pu_decode_gqa": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p,
                              _c_void_p, _c_void_p, _size_t, _i64, _i64, _i64, _i64, _i64, _float,
                              _float, _float, _c_void_p]),

@@ -151,7 +151,7 @@ def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch
     if grouped:
         o = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device=dev)
         lse = torch.empty((B, H), dtype=torch.float32, device=dev)
-        ws = DecodeWorkspace.get(dev, int(lib.pu_decode_workspace_size(B, H, n_local, D)))
+        ws = DecodeWorkspace.get(dev, int(lib.pu_decode_gqa_workspace_size(B, H, H_kv, n_local, D)))
         _lib.check(lib.pu_decode_gqa(q_.data_ptr(), _DT[q_.dtype], k_.data_ptr(), v_.data_ptr(),
                                      _DT_KV[k_.dtype],
                                      lens.data_ptr() if lens is not None else None,
