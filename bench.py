@@ -525,8 +525,10 @@ def _free_port() -> int:
 
 def bench_gqa_decode(steps: int, warmup: int):
     """Grouped-head decode on one GPU: B=1, 32 query heads over 8 K/V heads,
-    32768 tokens, D=128, fp16 and fp8 (e4m3) caches.  Returns
-    {dtype: (us, K/V bytes read)}."""
+    32768 tokens, D=128, fp16 (tensor-core kernel) and fp8 (e4m3, CUDA-core
+    kernel) caches; then the ragged batch of the decode_ragged leg (B=8,
+    lengths U[4096, 131072]) with 32 query heads over 8 K/V heads, fp16.
+    Returns {case: (us, K/V bytes read)}."""
     import torch
     from pallas_flash.kernels import decoding as dec
 
@@ -551,6 +553,22 @@ def bench_gqa_decode(steps: int, warmup: int):
         torch.cuda.synchronize()
         us = _timed(step, steps, flush, stream)
         out[name] = (us, 2 * kc.numel() * kc.element_size())
+    del caches, k, v
+    # ragged batch, grouped heads
+    Bg, Ng = RAG_B, RAG_NCAP
+    lens = ragged_lens()
+    qg = torch.randn((Bg, H, 1, D), device="cuda", generator=g).to(torch.float16)
+    kg = torch.randn((Bg, H_kv, Ng, D), device="cuda", generator=g).to(torch.float16)
+    vg = torch.randn((Bg, H_kv, Ng, D), device="cuda", generator=g).to(torch.float16)
+    lens_d = torch.tensor(lens, dtype=torch.int32, device="cuda")
+
+    def step_r():
+        return dec.pallas_flash_decoding(qg, kg, vg, kv_lens=lens_d)
+    for _ in range(warmup):
+        step_r()
+    torch.cuda.synchronize()
+    us = _timed(step_r, steps, flush, stream)
+    out["ragged_f16"] = (us, 2 * int(sum(lens)) * H_kv * D * 2)
     return out
 
 
@@ -682,7 +700,9 @@ def main():
                                   "direction (measured peer copy)"}}
         if gqa:
             line["decode_gqa"] = {
-                "workload": "grouped-head decode B=1 H=32 H_kv=8 N=32768 D=128, one GPU",
+                "workload": "grouped-head decode B=1 H=32 H_kv=8 N=32768 D=128, one GPU (f16: "
+                            "gqa_tc_kernel, tcgen05 K-tile x query-group; fp8_e4m3: gqa_kernel, CUDA "
+                            "cores); ragged_f16: B=8 H=32 H_kv=8 D=128 with the decode_ragged lengths",
                 "l2": "1 GiB buffer written, then another 1 GiB read, before every step"}
             for name, (us, nbytes) in gqa.items():
                 line["decode_gqa"][name] = {

@@ -253,56 +253,3 @@ inline bool gqa_grouped(long long H, long long H_kv) {
 
 }  // namespace decode
 }  // namespace pu
-
-extern "C" {
-
-size_t pu_decode_gqa_workspace_size(int64_t B, int64_t H, int64_t H_kv, int64_t n, int64_t D) {
-  using namespace pu::decode;
-  if (B <= 0 || H <= 0 || H_kv <= 0 || n <= 0 || D <= 0 || H % H_kv) return 0;
-  if (!gqa_grouped(H, H_kv)) return workspace_bytes_any(B * H, n, D, pu::sm_count());
-  return std::max(gqa_plan(B, H, H_kv, n, D, pu::sm_count(), false).total_bytes,
-                  gqa_plan(B, H, H_kv, n, D, pu::sm_count(), true).total_bytes);
-}
-
-int pu_decode_gqa(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
-                  const int32_t* kv_lens, void* o, float* lse, void* workspace, size_t workspace_bytes,
-                  int64_t B, int64_t H, int64_t H_kv, int64_t n, int64_t D, float sm_scale, float k_scale,
-                  float v_scale, void* stream) {
-  using namespace pu::decode;
-  int rc = check_args(q, q_dtype, k_cache, v_cache, kv_dtype, B, H, n, D, true);
-  if (rc) return rc;
-  if (!o) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null output");
-  if (H_kv <= 0 || H % H_kv != 0)
-    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "H = %lld is not a multiple of H_kv = %lld", (long long)H,
-                         (long long)H_kv);
-  if (!(k_scale > 0.f) || !(v_scale > 0.f) || !isfinite(k_scale) || !isfinite(v_scale))
-    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "k_scale and v_scale must be positive and finite");
-  const bool grouped = gqa_grouped(H, H_kv);
-  const Plan pl = grouped ? gqa_plan(B, H, H_kv, n, D, pu::sm_count(), kv_lens != nullptr)
-                          : make_plan(B * H, n, D, pu::sm_count(), kv_lens != nullptr);
-  if (!workspace || workspace_bytes < pl.total_bytes)
-    return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
-                         workspace_bytes);
-  Params prm{};
-  prm.q = q;
-  prm.k = k_cache;
-  prm.v = v_cache;
-  prm.lens = kv_lens;
-  prm.kv_offset = 0;
-  prm.n_local = (int)n;
-  prm.H = (int)H;
-  prm.group = (int)(H / H_kv);
-  prm.o_scale = v_scale;
-  prm.splits = pl.splits;
-  prm.chunk = pl.chunk;
-  prm.scale_log2 = sm_scale * k_scale * kLog2e;
-  prm.ws_rec = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.rec_off);
-  prm.ws_count = static_cast<int*>(workspace);
-  prm.o = static_cast<__nv_bfloat16*>(o);
-  prm.lse = lse;
-  if (grouped)
-    return launch_gqa(prm, q_dtype, kv_dtype, (int)D, prm.group, (int)(B * H_kv), static_cast<cudaStream_t>(stream));
-  return launch<true>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));
-}
-
-}  // extern "C"

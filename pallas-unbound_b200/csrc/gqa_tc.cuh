@@ -1,0 +1,619 @@
+// gqa_tc.cuh — grouped-head split-KV decode on the tensor core (D = 128,
+// q and cache of one 16-bit type, G = H / H_kv >= 2 query heads per K/V head).
+//
+// No counterpart in the reference (one K/V head per query head;
+// src/pallas_flash/kernels/decoding.py:105-115 is the per-head math).  One
+// CTA per (split, b, K/V head, slice of at most 16 query heads) streams its
+// chunk of the cache once, in tiles of 128 rows, and computes the heads of
+// its slice:
+//
+//   S   [128 rows x 16 heads] = K_tile · Qsᵀ      A = K tile (K-major), B = the
+//                                                slice's queries, zero-padded
+//   Oᵀ  [128 dims x 16 heads] += V_tileᵀ · Pᵀ     A = V tile read MN-major,
+//                                                B = Pᵀ (heads x rows, K-major)
+//
+// so the rows of the tile are the MMA's M and the heads its N: ~4·16·D flops
+// per cache row, far below what HBM delivers — the kernel is bound by the
+// K/V stream.  The slices of one K/V head are neighbouring CTAs that read the
+// same tiles at the same time (the repeats come from L2).
+//
+// Roles (256 threads):
+//   warp 4 lane 0  TMA producer: K and V tiles (2 x 16 KB boxes each) into an
+//                  NS-deep ring, one full/empty barrier pair per stage
+//   warp 5 lane 0  tcgen05 issuer: S_j as soon as tile j has landed (and
+//                  its S buffer is free), Oᵀ += V_jᵀ·P_jᵀ as soon as P_j is
+//                  written, whichever comes first; warp 5 also owns the
+//                  TMEM allocation
+//   warps 0-3      row r of the tile = TMEM lane r = thread r: scores in
+//                  log2 units, a running maximum per head shared by the CTA
+//                  that moves only when a score exceeds it by more than 8
+//                  (then Oᵀ and the partial sums are rescaled), P = 2^(s-m)
+//                  written as 16-bit into shared memory, partial sums l per
+//                  thread; at the end thread d reads row d of Oᵀ and the
+//                  split record of every head is written
+//   all            the last CTA of a (b, K/V head, slice) merges the split
+//                  records of its heads at once (weights in the idle ring)
+//
+// TMEM (64 columns): S_0 [0,16), S_1 [16,32), Oᵀ [32,48).
+// Rows past the chunk's end inside the last tile are masked to -inf; their V
+// rows are zeroed in shared memory before the P·V product (so stale cache
+// contents cannot reach the output).  Every wait is bounded; the softmax
+// warps run the same barrier sequence whatever a wait returns, so a timeout
+// ends the kernel with PU_ERR_DEVICE_TIMEOUT (detail 305) instead of a hang.
+#pragma once
+
+#include <algorithm>
+#include <type_traits>
+
+#include "gqa.cuh"
+
+namespace pu {
+namespace decode {
+namespace tc {
+
+constexpr int BT = 128;                    // cache rows per tile (MMA M)
+constexpr int kDim = 128;                  // head size
+constexpr int NS = 3;                      // K/V ring depth
+constexpr int kTileBytes = BT * kDim * 2;  // one K or V tile
+constexpr float kRescaleLog2 = 8.f;
+static_assert(kThreads == 256, "the softmax warps are 0-3, producer 4, issuer 5");
+
+template <int NP>
+struct Cfg {
+  static constexpr int kBlock = NP * 128;                  // bytes of one 64-column swizzle block
+  static constexpr int kQBytes = 2 * kBlock;               // query group [NP x 128], K-major
+  static constexpr int kPBytes = 2 * kBlock;               // Pᵀ [NP x 128 rows], K-major
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffP = kOffQ + kQBytes;            // two buffers
+  static constexpr int kOffKV = kOffP + 2 * kPBytes;       // stage s: K, then V
+  static constexpr int kOffBar = kOffKV + NS * 2 * kTileBytes;
+  // full[NS], empty[NS], s_full[2], p_full[2], p_free[2], drain
+  static constexpr int kNumBars = 2 * NS + 7;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem base, abort flag, last-CTA flag
+  static constexpr int kOffRed = kOffMisc + 16;            // [4][NP] floats
+  static constexpr int kSmemBytes = kOffRed + 4 * NP * 4;
+  static constexpr uint32_t kTmemCols = NP <= 16 ? 64 : 128;
+  static_assert(kOffP % 1024 == 0 && kPBytes % 1024 == 0 && kOffKV % 1024 == 0,
+                "swizzled operands start on 1024-byte boundaries");
+};
+
+template <int NP>
+__device__ __forceinline__ void tmem_ld_np(uint32_t taddr, uint32_t (&r)[NP]) {
+  if constexpr (NP == 16) tmem_ld16(taddr, r);
+  else tmem_ld32(taddr, r);
+}
+
+template <int NP>
+__device__ __forceinline__ void tmem_st_np(uint32_t taddr, const uint32_t (&r)[NP]) {
+  if constexpr (NP == 16) tmem_st16(taddr, r);
+  else tmem_st32(taddr, r);
+}
+
+template <typename T>
+__device__ __forceinline__ uint16_t to16(float x);
+template <>
+__device__ __forceinline__ uint16_t to16<__half>(float x) { return __half_as_ushort(__float2half_rn(x)); }
+template <>
+__device__ __forceinline__ uint16_t to16<__nv_bfloat16>(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// A group of more than NP query heads is cut into ceil(G / NP) slices of at
+// most NP heads, one CTA per slice; the CTAs of one (split, b, K/V head) are
+// neighbours in the grid and read the same K/V tiles at the same time, so
+// all but the first read come from L2.  The per-head loops run over NP with
+// the heads past the slice skipped.
+template <typename T, int NP>
+__global__ void __launch_bounds__(kThreads, 1)
+    gqa_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                  const Params p) {
+  using C = Cfg<NP>;
+  static_assert(NP == 16 || NP == 32, "padded group size");
+  const int Gt = p.group;                       // query heads per K/V head
+  const int n_slices = (Gt + NP - 1) / NP;
+  const int slice = (int)blockIdx.x % n_slices;
+  const int G = min(NP, Gt - slice * NP);       // this CTA's query heads
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (smem_u32(smem) & 1023u) {
+    if (tid == 0) record_device_error(PU_ERR_UNSUPPORTED, kSiteDecodeTc);
+    return;
+  }
+  uint8_t* sQ = smem + C::kOffQ;
+  uint8_t* sP = smem + C::kOffP;
+  uint8_t* sKV = smem + C::kOffKV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* bFull = bars;
+  uint64_t* bEmpty = bFull + NS;
+  uint64_t* bSf = bEmpty + NS;     // [2] S_j in TMEM
+  uint64_t* bPf = bSf + 2;         // [2] P_j in shared memory (128 arrivals)
+  uint64_t* bPfree = bPf + 2;      // [2] P_j·V_j done (P buffer free, Oᵀ settled)
+  uint64_t* bDrain = bPfree + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
+  int* sm_last = reinterpret_cast<int*>(smem + C::kOffMisc + 8);
+  float* sm_red4 = reinterpret_cast<float*>(smem + C::kOffRed);
+
+  const int split = (int)blockIdx.x / n_slices;
+  const int bkv = blockIdx.y;                   // b * H_kv + K/V head
+  const int H_kv = p.H / Gt;
+  const int b = bkv / H_kv;
+  const int bh0 = b * p.H + (bkv % H_kv) * Gt + slice * NP;   // this CTA's first query head
+  int len = p.n_local;
+  if (p.lens != nullptr) {
+    const long long g = (long long)p.lens[b];
+    len = g < 0 ? 0 : (g > p.n_local ? p.n_local : (int)g);
+  }
+  const int t_begin = split * p.chunk;
+  const int t_end = min(t_begin + p.chunk, len);
+  const int n_tiles = t_end > t_begin ? (t_end - t_begin + BT - 1) / BT : 0;
+
+  // query group -> sQ (K-major, 128-byte swizzle; rows G..NP-1 zero); both
+  // Pᵀ buffers zeroed (rows G..NP-1 are never written afterwards)
+  for (int c = tid; c < NP * 16; c += kThreads) {
+    const int n = c >> 4, cr = c & 15, cb = cr >> 3, ch = cr & 7;
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (n < G) w = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (size_t)(bh0 + n) * kDim + cr * 8);
+    *reinterpret_cast<uint4*>(sQ + cb * C::kBlock + n * 128 + ((ch ^ (n & 7)) << 4)) = w;
+  }
+  for (int c = tid; c < 2 * C::kPBytes / 16; c += kThreads)
+    reinterpret_cast<uint4*>(sP)[c] = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bFull + s, 1);
+      mbar_init(bEmpty + s, 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bSf + t, 1);
+      mbar_init(bPf + t, 128);
+      mbar_init(bPfree + t, 1);
+    }
+    mbar_init(bDrain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t col_o = 2 * NP;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int issued = 0;
+      for (int i = 0; i < n_tiles; ++i) {
+        const int s = i % NS;
+        const int u = i / NS;
+        if (u > 0 && !mbar_wait(bEmpty + s, (u - 1) & 1, abort_flag, kSiteDecodeTc)) break;
+        uint8_t* dK = sKV + s * 2 * kTileBytes;
+        uint8_t* dV = dK + kTileBytes;
+        const int row = t_begin + i * BT;
+        mbar_arrive_expect_tx(bFull + s, 2 * kTileBytes);
+        for (int cb = 0; cb < 2; ++cb) tma_load_3d(dK + cb * BT * 128, &tmK, bFull + s, cb * 64, row, bkv);
+        for (int cb = 0; cb < 2; ++cb) tma_load_3d(dV + cb * BT * 128, &tmV, bFull + s, cb * 64, row, bkv);
+        ++issued;
+      }
+      // copies still in flight land before the CTA may exit
+      volatile int no_abort = 0;
+      for (int i = max(0, issued - NS); i < issued; ++i)
+        mbar_wait(bFull + i % NS, (i / NS) & 1, &no_abort, kSiteDecodeTc);
+    }
+  } else if (warp == 5) {
+    // ---------------- tcgen05 issuer ----------------
+    if (lane == 0) {
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+      constexpr uint32_t idS = make_idesc_16(BT, NP, 0, 0, kBf16);
+      constexpr uint32_t idO = make_idesc_16(kDim, NP, 1, 0, kBf16);
+      const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t dP0 = make_sdesc_sw128(smem_u32(sP), 16, 1024);
+      const uint64_t dK0 = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
+      const uint64_t dV0 = make_sdesc_sw128(smem_u32(sKV + kTileBytes), BT * 128, 1024);
+      auto issue_S = [&](int j) {                // S_{j} into buffer j & 1 from stage j % NS
+        const uint64_t dk = sdesc_add(dK0, (j % NS) * 2 * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kDim / 16; ++kk) {
+          const uint32_t offk = (kk >> 2) * (BT * 128) + (kk & 3) * 32;
+          const uint32_t offq = (kk >> 2) * C::kBlock + (kk & 3) * 32;
+          mma_ss(tmem + (j & 1) * NP, sdesc_add(dk, offk), sdesc_add(dQ, offq), idS, kk > 0);
+        }
+        mma_commit(bSf + (j & 1));
+      };
+      // S_js and P_jp·V_jp are issued as soon as each is ready (polling both
+      // barriers), so a tile still in flight never holds back the P·V product
+      // that frees an earlier stage.  S_js overwrites S buffer js & 1, free
+      // once P_{js-2} was written, i.e. once P_{js-2}·V was issued: js <= jp + 1.
+      int js = 0, jp = 0;
+      uint64_t t_last = global_timer_ns();
+      while (jp < n_tiles) {
+        bool progressed = false;
+        if (js < n_tiles && js <= jp + 1 && mbar_try_wait(smem_u32(bFull + js % NS), (js / NS) & 1)) {
+          tc_fence_after();
+          issue_S(js);
+          ++js;
+          progressed = true;
+        }
+        if (jp < js && mbar_try_wait(smem_u32(bPf + (jp & 1)), (jp >> 1) & 1)) {
+          tc_fence_after();
+          const uint64_t dv = sdesc_add(dV0, (jp % NS) * 2 * kTileBytes);
+          const uint64_t dp = sdesc_add(dP0, (jp & 1) * C::kPBytes);
+#pragma unroll
+          for (int kk = 0; kk < BT / 16; ++kk) {
+            const uint32_t offp = (kk >> 2) * C::kBlock + (kk & 3) * 32;
+            mma_ss(tmem + col_o, sdesc_add(dv, kk * 16 * 128), sdesc_add(dp, offp), idO, (jp > 0 || kk > 0));
+          }
+          mma_commit(bPfree + (jp & 1));
+          mma_commit(bEmpty + jp % NS);
+          ++jp;
+          progressed = true;
+        }
+        if (progressed) {
+          t_last = global_timer_ns();
+        } else {
+          if (*abort_flag) break;
+          if (global_timer_ns() - t_last > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            record_device_error(PU_ERR_DEVICE_TIMEOUT, kSiteDecodeTc);
+            break;
+          }
+        }
+      }
+      // every issued product completes before TMEM and shared memory go away
+      mma_commit(bDrain);
+      volatile int no_abort = 0;
+      mbar_wait(bDrain, 0, &no_abort, kSiteDecodeTc);
+    }
+  } else if (warp < 4) {
+    // ---------------- rows / heads (warps 0-3) ----------------
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    float m_run[NP], l_part[NP];
+#pragma unroll
+    for (int h = 0; h < NP; ++h) {
+      m_run[h] = -INFINITY;
+      l_part[h] = 0.f;
+    }
+    const int kb = tid >> 6, kc = tid & 63;       // this row's place in a Pᵀ row
+    const uint32_t p_off = kb * C::kBlock + (kc & 7) * 2;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int buf = j & 1;
+      mbar_wait(bSf + buf, (j >> 1) & 1, abort_flag, kSiteDecodeTc);
+      __syncwarp();
+      tc_fence_after();
+      uint32_t r[NP];
+      tmem_ld_np<NP>(tmem + lane_base + buf * NP, r);
+      tmem_wait_ld();
+      reg_fence(r);
+      const int tile0 = t_begin + j * BT;
+      const bool valid = tile0 + tid < t_end;
+      float s[NP];
+      bool up = false;
+#pragma unroll
+      for (int h = 0; h < NP; ++h) {
+        s[h] = valid ? __uint_as_float(r[h]) * p.scale_log2 : -INFINITY;
+        if (h < G) up |= s[h] > m_run[h] + kRescaleLog2;
+      }
+      if (bar_any_named(1, 128, up)) {
+        // the tile's maximum of each head over all 128 rows
+#pragma unroll
+        for (int h = 0; h < NP; ++h) {
+          if (h >= G) break;
+          float v = s[h];
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+          if (lane == 0) sm_red4[warp * NP + h] = v;
+        }
+        bar_sync_named(1, 128);
+        float alpha[NP];
+#pragma unroll
+        for (int h = 0; h < NP; ++h) {
+          alpha[h] = 1.f;
+          if (h >= G) continue;
+          const float tm = fmaxf(fmaxf(sm_red4[h], sm_red4[NP + h]), fmaxf(sm_red4[2 * NP + h], sm_red4[3 * NP + h]));
+          if (tm > m_run[h] + kRescaleLog2) {      // same decision in every thread
+            alpha[h] = (m_run[h] == -INFINITY) ? 0.f : ex2(m_run[h] - tm);
+            m_run[h] = tm;
+          }
+          l_part[h] *= alpha[h];
+        }
+        if (j > 0) {
+          // Oᵀ holds tiles < j once P_{j-1}·V_{j-1} is done; row tid of Oᵀ is
+          // this thread's TMEM lane
+          mbar_wait(bPfree + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, kSiteDecodeTc);
+          __syncwarp();
+          tc_fence_after();
+          uint32_t ov[NP];
+          tmem_ld_np<NP>(tmem + lane_base + col_o, ov);
+          tmem_wait_ld();
+          reg_fence(ov);
+#pragma unroll
+          for (int h = 0; h < NP; ++h) ov[h] = __float_as_uint(__uint_as_float(ov[h]) * alpha[h]);
+          tmem_st_np<NP>(tmem + lane_base + col_o, ov);
+          tmem_wait_st();
+        }
+      }
+      // the last tile: rows past the chunk's end get zero V rows
+      if (!valid) {
+        mbar_wait(bFull + j % NS, (j / NS) & 1, abort_flag, kSiteDecodeTc);
+        uint8_t* vrow = sKV + (j % NS) * 2 * kTileBytes + kTileBytes + tid * 128;
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb)
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            reinterpret_cast<uint4*>(vrow + cb * BT * 128)[c] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      // P_j into buffer `buf` once P_{j-2}·V_{j-2} has read it
+      if (j >= 2) mbar_wait(bPfree + buf, ((j - 2) >> 1) & 1, abort_flag, kSiteDecodeTc);
+      uint8_t* pb = sP + buf * C::kPBytes + p_off;
+#pragma unroll
+      for (int h = 0; h < NP; ++h) {
+        if (h >= G) break;
+        const float pr = ex2(s[h] - m_run[h]);     // 0 for masked rows
+        l_part[h] += pr;
+        *reinterpret_cast<uint16_t*>(pb + h * 128 + (((kc >> 3) ^ (h & 7)) << 4)) = to16<T>(pr);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bPf + buf);
+      __syncwarp();
+    }
+
+    // split record of every head: m (log2 units), l, o[d] (thread d)
+    float o[NP];
+#pragma unroll
+    for (int h = 0; h < NP; ++h) o[h] = 0.f;
+    if (n_tiles > 0) {
+      mbar_wait(bPfree + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, abort_flag, kSiteDecodeTc);
+      __syncwarp();
+      tc_fence_after();
+      uint32_t ov[NP];
+      tmem_ld_np<NP>(tmem + lane_base + col_o, ov);
+      tmem_wait_ld();
+      reg_fence(ov);
+#pragma unroll
+      for (int h = 0; h < NP; ++h) o[h] = __uint_as_float(ov[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < NP; ++h) {
+      if (h >= G) break;
+      float v = l_part[h];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) sm_red4[warp * NP + h] = v;
+    }
+    bar_sync_named(1, 128);
+#pragma unroll
+    for (int h = 0; h < NP; ++h) {
+      if (h >= G) break;
+      float* rec = p.ws_rec + ((size_t)(bh0 + h) * p.splits + split) * (kDim + 2);
+      rec[2 + tid] = o[h] * p.o_scale;
+      if (tid == 0) {
+        rec[0] = m_run[h];
+        rec[1] = (sm_red4[h] + sm_red4[NP + h]) + (sm_red4[2 * NP + h] + sm_red4[3 * NP + h]);
+      }
+    }
+    __threadfence();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+  __threadfence();
+  if (tid == 0) {
+    const int prev = atomicAdd(p.ws_count + bkv * n_slices + slice, 1);
+    *sm_last = (prev == p.splits - 1);
+  }
+  __syncthreads();
+  if (!*sm_last) return;
+  __threadfence();
+  // last CTA of this (b, K/V head, slice): merge the split records of its G
+  // query heads at once (the records of heads bh0.. are contiguous); the K/V ring
+  // is idle now and holds the merge weights
+  const int S = p.splits;
+  const float* recs = p.ws_rec + (size_t)bh0 * S * (kDim + 2);
+  float* sw = reinterpret_cast<float*>(sKV);    // [G][S]
+  float* sML = sw + G * S;                      // M [G], then L [G]
+  for (int h = warp; h < G; h += kWarps) {      // one warp per head
+    const float* rh = recs + (size_t)h * S * (kDim + 2);
+    float mx = -INFINITY;
+    for (int s = lane; s < S; s += 32) mx = fmaxf(mx, __ldcg(rh + (size_t)s * (kDim + 2)));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float ls = 0.f;
+    for (int s = lane; s < S; s += 32) {
+      const float m = __ldcg(rh + (size_t)s * (kDim + 2));
+      const float w = (m == -INFINITY) ? 0.f : ex2(m - mx);   // every record empty: all 0
+      sw[h * S + s] = w;
+      ls += w * __ldcg(rh + (size_t)s * (kDim + 2) + 1);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+    if (lane == 0) {
+      sML[h] = mx;
+      sML[G + h] = ls;
+    }
+  }
+  __syncthreads();
+  // outputs (h, d) two per thread and pass, 8 records of each in flight,
+  // summed in record order
+  for (int ia = tid; ia < G * kDim; ia += 2 * kThreads) {
+    const int ib = ia + kThreads;
+    const bool two = ib < G * kDim;             // the same in a whole warp
+    const int ha = ia / kDim, da = ia % kDim;
+    const int hb = two ? ib / kDim : ha, db = two ? ib % kDim : da;
+    const float* pa = recs + (size_t)ha * S * (kDim + 2) + 2 + da;
+    const float* pb = recs + (size_t)hb * S * (kDim + 2) + 2 + db;
+    const float* wa = sw + ha * S;
+    const float* wb = sw + hb * S;
+    float aa = 0.f, ab = 0.f;
+    int s = 0;
+    for (; s + 8 <= S; s += 8) {
+      float xa[8], xb[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        xa[u] = __ldcg(pa + (size_t)(s + u) * (kDim + 2));
+        xb[u] = __ldcg(pb + (size_t)(s + u) * (kDim + 2));
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        aa = fmaf(wa[s + u], xa[u], aa);
+        ab = fmaf(wb[s + u], xb[u], ab);
+      }
+    }
+    for (; s < S; ++s) {
+      aa = fmaf(wa[s], __ldcg(pa + (size_t)s * (kDim + 2)), aa);
+      ab = fmaf(wb[s], __ldcg(pb + (size_t)s * (kDim + 2)), ab);
+    }
+    const float La = sML[G + ha];
+    p.o[(size_t)(bh0 + ha) * kDim + da] = __float2bfloat16_rn(La > 0.f ? aa / La : 0.f);
+    if (two) {
+      const float Lb = sML[G + hb];
+      p.o[(size_t)(bh0 + hb) * kDim + db] = __float2bfloat16_rn(Lb > 0.f ? ab / Lb : 0.f);
+    }
+  }
+  if (tid < G && p.lse != nullptr) {
+    const float L = sML[G + tid];
+    p.lse[bh0 + tid] = (L > 0.f) ? (sML[tid] + lg2(L)) * kLn2 : -INFINITY;
+  }
+  if (tid == 0) p.ws_count[bkv * n_slices + slice] = 0;  // leave the workspace zeroed for the next call
+}
+
+// The tensor-core kernel takes D = 128, q and cache of the same 16-bit type
+// and G >= 2.
+constexpr int kSliceHeads = 16;   // query heads per CTA (the MMA's N)
+
+inline bool tc_eligible(long long H, long long H_kv, long long D, int q_dtype, int kv_dtype) {
+  return D == kDim && q_dtype == kv_dtype && (kv_dtype == PU_DTYPE_F16 || kv_dtype == PU_DTYPE_BF16) &&
+         H / H_kv >= 2;
+}
+
+inline long long n_slices(long long G) { return (G + kSliceHeads - 1) / kSliceHeads; }
+
+// Split records one last CTA merges (heads x splits): more splits spread the
+// stream over more SMs, but the merge runs on one SM (256 measured best of
+// 64-1024 over G = 2-32, B = 1-8).
+constexpr long long kMaxRecords = 256;
+
+// One CTA per SM; chunks are whole tiles; at most kMaxRecords / (heads of a
+// slice) splits (the merge weights, heads x splits floats, fit in the idle
+// K/V ring).
+inline Plan tc_plan(long long B, long long H, long long H_kv, long long n, int num_sms, bool ragged) {
+  const long long G = H / H_kv;
+  Plan pl = make_plan(B * H_kv * n_slices(G), n, kDim, num_sms / kCtasPerSm > 0 ? num_sms / kCtasPerSm : 1,
+                      ragged, BT);
+  const long long cap = std::max<long long>(1, kMaxRecords / std::min<long long>(G, kSliceHeads));
+  if (pl.splits > cap) {
+    const long long chunk = ((n + cap - 1) / cap + BT - 1) / BT * BT;
+    pl.chunk = (int)chunk;
+    pl.splits = (int)((n + chunk - 1) / chunk);
+  }
+  pl.total_bytes = pl.rec_off + round_up((size_t)B * H * pl.splits * (kDim + 2) * sizeof(float), 256);
+  return pl;
+}
+
+template <typename T, int NP>
+int launch_np(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, dim3 grid, cudaStream_t st) {
+  constexpr int smem = Cfg<NP>::kSmemBytes;
+  static bool configured = false;   // per instantiation; the attribute is per function
+  if (!configured) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(gqa_tc_kernel<T, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return check_cuda(e, "grouped-head decode (tensor core) shared memory");
+    configured = true;
+  }
+  gqa_tc_kernel<T, NP><<<grid, kThreads, smem, st>>>(tk, tv, prm);
+  return check_cuda(cudaGetLastError(), "grouped-head decode (tensor core) launch");
+}
+
+inline int launch(const Params& prm, int kv_dtype, long long B, long long H_kv, cudaStream_t st) {
+  if ((long long)kSliceHeads * prm.splits + 2 * kSliceHeads > NS * 2 * kTileBytes / 4)
+    return set_error(PU_ERR_UNSUPPORTED, "grouped-head decode: %d splits exceed the merge space", prm.splits);
+  CUtensorMap tk, tv;
+  int rc = make_tmap_bf16_3d(&tk, prm.k, kDim, prm.n_local, B * H_kv, 64, BT, true);
+  if (!rc) rc = make_tmap_bf16_3d(&tv, prm.v, kDim, prm.n_local, B * H_kv, 64, BT, true);
+  if (rc) return rc;
+  const dim3 grid((unsigned)(prm.splits * n_slices(prm.group)), (unsigned)(B * H_kv));
+  return kv_dtype == PU_DTYPE_F16 ? launch_np<__half, kSliceHeads>(tk, tv, prm, grid, st)
+                                  : launch_np<__nv_bfloat16, kSliceHeads>(tk, tv, prm, grid, st);
+}
+
+}  // namespace tc
+}  // namespace decode
+}  // namespace pu
+
+extern "C" {
+
+// Serves every kernel pu_decode_gqa may pick for these sizes (with or
+// without lengths, any dtypes).
+size_t pu_decode_gqa_workspace_size(int64_t B, int64_t H, int64_t H_kv, int64_t n, int64_t D) {
+  using namespace pu::decode;
+  if (B <= 0 || H <= 0 || H_kv <= 0 || n <= 0 || D <= 0 || H % H_kv) return 0;
+  const int sms = pu::sm_count();
+  size_t bytes = workspace_bytes_any(B * H, n, D, sms);
+  if (gqa_grouped(H, H_kv))
+    bytes = std::max({bytes, gqa_plan(B, H, H_kv, n, D, sms, false).total_bytes,
+                      gqa_plan(B, H, H_kv, n, D, sms, true).total_bytes});
+  if (tc::tc_eligible(H, H_kv, D, PU_DTYPE_F16, PU_DTYPE_F16))
+    bytes = std::max({bytes, tc::tc_plan(B, H, H_kv, n, sms, false).total_bytes,
+                      tc::tc_plan(B, H, H_kv, n, sms, true).total_bytes});
+  return bytes;
+}
+
+int pu_decode_gqa(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
+                  const int32_t* kv_lens, void* o, float* lse, void* workspace, size_t workspace_bytes,
+                  int64_t B, int64_t H, int64_t H_kv, int64_t n, int64_t D, float sm_scale, float k_scale,
+                  float v_scale, void* stream) {
+  using namespace pu::decode;
+  int rc = check_args(q, q_dtype, k_cache, v_cache, kv_dtype, B, H, n, D, true);
+  if (rc) return rc;
+  if (!o) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null output");
+  if (H_kv <= 0 || H % H_kv != 0)
+    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "H = %lld is not a multiple of H_kv = %lld", (long long)H,
+                         (long long)H_kv);
+  if (!(k_scale > 0.f) || !(v_scale > 0.f) || !isfinite(k_scale) || !isfinite(v_scale))
+    return pu::set_error(PU_ERR_INVALID_ARGUMENT, "k_scale and v_scale must be positive and finite");
+  // tensor core for 16-bit caches with D = 128 and 2 <= G <= 32; the
+  // CUDA-core grouped kernel for fp8 caches, D = 64 or mixed dtypes (G = 2,
+  // 4, 8); otherwise the query-head kernel reading K/V head h / G
+  const bool on_tc = tc::tc_eligible(H, H_kv, D, q_dtype, kv_dtype);
+  const bool grouped = !on_tc && gqa_grouped(H, H_kv);
+  const bool ragged = kv_lens != nullptr;
+  const Plan pl = on_tc ? tc::tc_plan(B, H, H_kv, n, pu::sm_count(), ragged)
+                        : grouped ? gqa_plan(B, H, H_kv, n, D, pu::sm_count(), ragged)
+                                  : make_plan(B * H, n, D, pu::sm_count(), ragged);
+  if (!workspace || workspace_bytes < pl.total_bytes)
+    return pu::set_error(PU_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", pl.total_bytes,
+                         workspace_bytes);
+  Params prm{};
+  prm.q = q;
+  prm.k = k_cache;
+  prm.v = v_cache;
+  prm.lens = kv_lens;
+  prm.kv_offset = 0;
+  prm.n_local = (int)n;
+  prm.H = (int)H;
+  prm.group = (int)(H / H_kv);
+  prm.o_scale = v_scale;
+  prm.splits = pl.splits;
+  prm.chunk = pl.chunk;
+  prm.scale_log2 = sm_scale * k_scale * kLog2e;
+  prm.ws_rec = reinterpret_cast<float*>(static_cast<char*>(workspace) + pl.rec_off);
+  prm.ws_count = static_cast<int*>(workspace);
+  prm.o = static_cast<__nv_bfloat16*>(o);
+  prm.lse = lse;
+  if (on_tc) return tc::launch(prm, kv_dtype, B, H_kv, static_cast<cudaStream_t>(stream));
+  if (grouped)
+    return launch_gqa(prm, q_dtype, kv_dtype, (int)D, prm.group, (int)(B * H_kv), static_cast<cudaStream_t>(stream));
+  return launch<true>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -4,7 +4,7 @@
 #include "capi.cuh"
 #include "decode.cuh"
 #include "paged.cuh"
-#include "gqa.cuh"
+#include "gqa_tc.cuh"
 #include "peer.cuh"
 #include "outproj.cuh"
 #include "attn_fwd.cuh"

@@ -92,6 +92,28 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // ---------------------------------------------------------------------------
+// Named barriers over a subset of the CTA's warps (id 1..15; count a
+// multiple of 32, every thread of those warps takes part)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bar_sync_named(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Barrier that also returns whether `pred` held in any participating thread.
+__device__ __forceinline__ bool bar_any_named(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+// ---------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -402,6 +424,14 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, int a_mn_ma
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
          (static_cast<uint32_t>(b_mn_major) << 16) | ((static_cast<uint32_t>(N) >> 3) << 17) |
          ((static_cast<uint32_t>(M) >> 4) << 24);
+}
+
+// Same for either 16-bit input type (`bf16` false: f16 A and B).
+__host__ __device__ constexpr uint32_t make_idesc_16(int M, int N, int a_mn_major, int b_mn_major,
+                                                     bool bf16) {
+  return (1u << 4) | (bf16 ? ((1u << 7) | (1u << 10)) : 0u) |
+         (static_cast<uint32_t>(a_mn_major) << 15) | (static_cast<uint32_t>(b_mn_major) << 16) |
+         ((static_cast<uint32_t>(N) >> 3) << 17) | ((static_cast<uint32_t>(M) >> 4) << 24);
 }
 
 }  // namespace pu

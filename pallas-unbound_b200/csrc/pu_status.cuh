@@ -40,6 +40,7 @@ enum WaitSite : int {
   kSiteDecodePage = 302,
   kSiteAppendPage = 303,
   kSiteDecodePeer = 304,
+  kSiteDecodeTc = 305,
   kSiteOutProj = 401,
   kSiteSelfTest = 901,
 };

@@ -2,12 +2,17 @@
 (pu_decode_gqa), against the oracle and against the MHA kernel on a cache
 whose K/V heads are repeated.
 
-  * H_kv in {H/2, H/4, H/8}: the grouped kernel (one CTA per K/V head for
-    all its query heads) against pu_decode on the repeated cache and the
-    oracle; H_kv = 1 with 16 query heads runs the query-head kernel, whose
+  * G = H / H_kv from 2 to 64 with q and cache of one 16-bit type and
+    D = 128: the tensor-core kernel (K tile x query slice, Vᵀ x Pᵀ; groups
+    above 16 heads in slices of 16) against pu_decode on the repeated cache
+    and the oracle; D = 64 with G = 16 runs the query-head kernel, whose
     split plan equals pu_decode's, so there the results match bit for bit
+  * the CUDA-core grouped kernel (mixed q / cache dtypes, D = 64, G = 2, 4, 8)
   * fp16 / bf16 caches, ragged lengths (0, 1, partial chunks), D 64 / 128:
     vs the oracle (o max-abs 2e-2 / rel 1e-2, LSE 1e-3)
+  * cache rows past a sequence's length holding NaN / Inf do not reach the
+    output; scores that keep growing along the sequence (the running
+    maximum moves many times, with rescales of the accumulated output)
   * fp8 (e4m3) caches with per-tensor scales: vs the oracle on the
     dequantised values (the same tolerance)
 """
@@ -45,12 +50,15 @@ def _f(t):
     return t.detach().float().cpu().numpy()
 
 
-@pytest.mark.parametrize("H,H_kv,dt", [(16, 8, torch.float16), (16, 4, torch.bfloat16),
-                                        (32, 4, torch.float16), (64, 8, torch.bfloat16),
-                                        (16, 1, torch.bfloat16)])
-def test_gqa_equals_repeated_cache(mods, H, H_kv, dt):
+@pytest.mark.parametrize("H,H_kv,dt,D", [(16, 8, torch.float16, 128), (16, 4, torch.bfloat16, 128),
+                                          (32, 4, torch.float16, 128), (64, 8, torch.bfloat16, 128),
+                                          (24, 8, torch.float16, 128), (16, 1, torch.bfloat16, 128),
+                                          (48, 2, torch.float16, 128), (32, 1, torch.float16, 128),
+                                          (40, 1, torch.bfloat16, 128), (64, 1, torch.float16, 128),
+                                          (16, 1, torch.bfloat16, 64)])
+def test_gqa_equals_repeated_cache(mods, H, H_kv, dt, D):
     _lib, dec = mods
-    B, N, D = 3, 3000, 128
+    B, N = 3, 3000
     q = _gen((B, H, 1, D), 1, dt)
     k = _gen((B, H_kv, N, D), 2, dt)
     v = _gen((B, H_kv, N, D), 3, dt)
@@ -61,7 +69,7 @@ def test_gqa_equals_repeated_cache(mods, H, H_kv, dt):
     o2, lse2 = dec.pallas_flash_decoding(q, kr, vr, kv_lens=lens, return_lse=True)
     torch.cuda.synchronize()
     assert _lib.device_status() == (0, 0)
-    if G in (2, 4, 8):
+    if D == 128:
         assert_close_o(_f(o), _f(o2), max_abs=1e-2, rel=5e-3, what="grouped vs repeated cache")
         live = lens.cpu().numpy() > 0
         assert_close_lse(_f(lse)[live], _f(lse2)[live], tol=1e-4)
@@ -72,11 +80,12 @@ def test_gqa_equals_repeated_cache(mods, H, H_kv, dt):
     assert_close_lse(_f(lse), rl)
 
 
-@pytest.mark.parametrize("D,H,H_kv", [(64, 8, 2), (128, 32, 8)])
-def test_gqa_vs_oracle(mods, D, H, H_kv):
+@pytest.mark.parametrize("D,H,H_kv,qdt", [(64, 8, 2, torch.bfloat16), (128, 32, 8, torch.bfloat16),
+                                          (128, 32, 8, torch.float16)])
+def test_gqa_vs_oracle(mods, D, H, H_kv, qdt):
     _lib, dec = mods
     B, N = 4, 2100
-    q = _gen((B, H, 1, D), 10 + D, torch.bfloat16)
+    q = _gen((B, H, 1, D), 10 + D, qdt)
     k = _gen((B, H_kv, N, D), 11 + D, torch.float16)
     v = _gen((B, H_kv, N, D), 12 + D, torch.float16)
     lens = torch.tensor([2100, 0, 257, 64], dtype=torch.int32, device="cuda")
@@ -112,4 +121,50 @@ def test_fp8_cache_vs_oracle(mods, H, H_kv):
     vd = _f(v8) * v_scale
     ro, rl = orc.decode_forward(_f(q), kd, vd, kv_lens=lens.cpu().numpy(), scale=1 / math.sqrt(D))
     assert_close_o(_f(o), ro, what="fp8 cache")
+    assert_close_lse(_f(lse), rl)
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gqa_stale_rows_past_length(mods, dt):
+    """Rows past each sequence's length hold NaN and Inf (stale or never
+    written cache slots): the output equals the oracle on the live rows."""
+    _lib, dec = mods
+    B, H, H_kv, N, D = 3, 32, 8, 1000, 128
+    q = _gen((B, H, 1, D), 40, dt)
+    k = _gen((B, H_kv, N, D), 41, dt)
+    v = _gen((B, H_kv, N, D), 42, dt)
+    lens = torch.tensor([1000, 130, 555], dtype=torch.int32, device="cuda")
+    for b, n in enumerate(lens.tolist()):
+        k[b, :, n:] = float("nan")
+        v[b, :, n:] = float("inf")
+    o, lse = dec.pallas_flash_decoding(q, k, v, kv_lens=lens, return_lse=True)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == (0, 0)
+    assert torch.isfinite(o).all() and torch.isfinite(lse).all()
+    kz, vz = k.clone(), v.clone()
+    for b, n in enumerate(lens.tolist()):
+        kz[b, :, n:] = 0
+        vz[b, :, n:] = 0
+    ro, rl = orc.decode_forward(_f(q), _f(kz), _f(vz), kv_lens=lens.cpu().numpy())
+    assert_close_o(_f(o), ro, what="stale rows")
+    assert_close_lse(_f(lse), rl)
+
+
+def test_gqa_growing_scores(mods):
+    """K rows scaled up along the sequence, so each tile's scores exceed the
+    running maximum of the previous ones and the output accumulated so far is
+    rescaled again and again; per head the growth differs."""
+    _lib, dec = mods
+    B, H, H_kv, N, D = 2, 16, 4, 4096, 128
+    dt = torch.float16
+    q = _gen((B, H, 1, D), 50, dt)
+    ramp = torch.linspace(0.2, 4.0, N, device="cuda").view(1, 1, N, 1)
+    k = (_gen((B, H_kv, N, D), 51, torch.float32) * 0.3 + 0.5 * q.float().view(B, H_kv, H // H_kv, D)[:, :, :1, :]) * ramp
+    k = k.to(dt)
+    v = _gen((B, H_kv, N, D), 52, dt)
+    o, lse = dec.pallas_flash_decoding(q, k, v, return_lse=True)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == (0, 0)
+    ro, rl = orc.decode_forward(_f(q), _f(k), _f(v))
+    assert_close_o(_f(o), ro, what="growing scores")
     assert_close_lse(_f(lse), rl)
