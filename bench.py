@@ -572,6 +572,28 @@ def bench_gqa_decode(steps: int, warmup: int):
     return out
 
 
+def profile_gqa(steps: int, warmup: int) -> float:
+    """The fp16 case of the grouped-head leg alone (B=1, H=32 over 8 K/V
+    heads, 32768 tokens), for ncu captures."""
+    import torch
+    from pallas_flash.kernels import decoding as dec
+
+    B, H, H_kv, N, D = 1, 32, 8, 32768, 128
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5000)
+    q = torch.randn((B, H, 1, D), device="cuda", generator=g).to(torch.float16)
+    k = torch.randn((B, H_kv, N, D), device="cuda", generator=g).to(torch.float16)
+    v = torch.randn((B, H_kv, N, D), device="cuda", generator=g).to(torch.float16)
+    flush = L2Flush()
+
+    def step():
+        return dec.pallas_flash_decoding(q, k, v)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    return _timed(step, steps, flush, torch.cuda.current_stream())
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -579,7 +601,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["pu", "reference"], default="pu")
     ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--profile-leg", choices=["attn", "decode"], default=None,
+    ap.add_argument("--profile-leg", choices=["attn", "decode", "gqa"], default=None,
                     help="run only this leg and print no JSON (small runs for ncu captures)")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
@@ -593,6 +615,10 @@ def main():
     if args.profile_leg == "decode":
         us, _, _ = bench_decode(args.steps, warmup, rank, world, "peer")
         print(f"decode leg: {us:.1f} us/step", flush=True)
+        return
+    if args.profile_leg == "gqa":
+        us = profile_gqa(args.steps, warmup)
+        print(f"grouped-head decode leg: {us:.1f} us/step", flush=True)
         return
     clocks = ClockSampler(local).start()
     total_ms, fwd_ms, bwd_ms = bench_attention(args.steps, warmup, rank, world, clocks)
