@@ -276,6 +276,46 @@ def bench_attention(steps: int, warmup: int, rank: int, world: int, clocks: Cloc
     return total_ms, fwd_ms, bwd_ms
 
 
+LONG_B, LONG_H, LONG_N = 1, 32, 16384
+LONG_FWD_FLOPS = 4 * LONG_B * LONG_H * LONG_N * LONG_N * D      # non-causal
+
+
+def bench_attention_long(steps: int, warmup: int):
+    """Non-causal long-sequence fwd+bwd on one GPU: B=1, H=32, N=16384,
+    D=128, Q/K/V ~ N(0, 0.5), dO ~ N(0, 1) (bf16).  Returns (fwd_ms, bwd_ms)
+    per step (medians)."""
+    import torch
+    from pallas_flash.ops import interface as pf
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3000)
+    shape = (LONG_B, LONG_H, LONG_N, D)
+    q, k, v = ((torch.randn(shape, device="cuda", generator=g) * 0.5).to(torch.bfloat16) for _ in range(3))
+    do = torch.randn(shape, device="cuda", generator=g).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    lse = torch.empty((LONG_B, LONG_H, LONG_N), device="cuda", dtype=torch.float32)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws = torch.empty(pf.bwd_workspace_bytes(LONG_B, LONG_H, LONG_N, D), device="cuda", dtype=torch.uint8)
+    stream = torch.cuda.current_stream()
+    fwd, bwd = [], []
+    for i in range(warmup + steps):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record(stream)
+        pf.flash_attention_forward(q, k, v, causal=False, out=o, lse=lse)
+        e[1].record(stream)
+        pf.flash_attention_backward(q, k, v, o, lse, do, causal=False, workspace=ws, dq=dq, dk=dk, dv=dv)
+        e[2].record(stream)
+        torch.cuda.synchronize()
+        if i >= warmup:
+            fwd.append(e[0].elapsed_time(e[1]))
+            bwd.append(e[1].elapsed_time(e[2]))
+    from pallas_flash import _lib
+    code, detail = _lib.device_status()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at site {detail}")
+    return statistics.median(fwd), statistics.median(bwd)
+
+
 def bench_attention_e2e(steps: int, warmup: int, rank: int, world: int):
     """Through the public API with host (pinned) tensors: H2D of q, k, v, dO and
     D2H of o, dq, dk, dv inside every timed step (torch.autograd drives the
@@ -637,6 +677,7 @@ def main():
     rag_us, rag_paged_us, rag_bytes = bench_ragged_decode(max(5, min(args.steps, 20)), warmup,
                                                           rank, world)
     gqa = bench_gqa_decode(max(5, min(args.steps, 50)), warmup) if world == 1 else None
+    long_ms = bench_attention_long(max(3, min(args.steps, 5)), warmup) if world == 1 else None
     op = bench_outproj(max(5, min(args.steps, 20)), warmup, rank, world)
 
     if rank == 0:
@@ -724,6 +765,16 @@ def main():
                          "frac": round(op_floor_us / op["peer"], 4),
                          "peaks": f"{peaks['bf16_tflops']} TFLOP/s bf16 (measured), 770 GB/s NVLink per "
                                   "direction (measured peer copy)"}}
+        if long_ms:
+            lf, lb = long_ms
+            line["attn_long"] = {
+                "workload": f"non-causal fwd+bwd B={LONG_B} H={LONG_H} N={LONG_N} D={D} bf16, "
+                            "Q/K/V ~ N(0,0.5), dO ~ N(0,1), one GPU",
+                "fwd_ms": round(lf, 3), "bwd_ms": round(lb, 3),
+                "TFLOP_s": round(LONG_FWD_FLOPS * 3.5 / ((lf + lb) * 1e-3) / 1e12, 1),
+                "fwd_TFLOP_s": round(LONG_FWD_FLOPS / (lf * 1e-3) / 1e12, 1),
+                "bwd_TFLOP_s": round(LONG_FWD_FLOPS * 2.5 / (lb * 1e-3) / 1e12, 1),
+                "frac": round(LONG_FWD_FLOPS * 3.5 / ((lf + lb) * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
         if gqa:
             line["decode_gqa"] = {
                 "workload": "grouped-head decode B=1 H=32 H_kv=8 N=32768 D=128, one GPU (f16: "

@@ -9,9 +9,11 @@ additions (defaults keep the reference's behaviour): `causal`,
 `sm_scale` (default 1/sqrt(D)), `return_lse`.  It is differentiable: the
 backward pass (which the reference lacks) reuses the saved LSE.
 
-Inputs may live on the GPU (the usual case) or on the host; host tensors are
-copied to the current CUDA device and the results copied back.  Every
-compute step runs in libpu_attn.so (sm_100a); there is no CPU fallback.
+Inputs may live on the GPU (the usual case) or on the host.  Host tensors are
+copied to the current CUDA device (asynchronously when they are pinned), and
+`o`, the LSE and, in the backward pass, dq / dk / dv come back as pinned host
+tensors (one stream synchronisation per call).  Every compute step runs in
+libpu_attn.so (sm_100a); there is no CPU fallback.
 """
 from __future__ import annotations
 
@@ -119,6 +121,48 @@ class _FlashAttention(torch.autograd.Function):
         return dq, dk, dv, None, None
 
 
+def _to_host(t: torch.Tensor) -> torch.Tensor:
+    """Asynchronous copy of a device tensor into a new pinned host tensor
+    (torch's pinned caching allocator reuses freed blocks)."""
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h.copy_(t, non_blocking=True)
+    return h
+
+
+class _HostFlashAttention(torch.autograd.Function):
+    """The attention of host tensors: inputs to the device, o / LSE and the
+    gradients back into pinned host memory.  The device copies of q, k, v, o
+    and the LSE are kept for the backward pass."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal, sm_scale, dev):
+        D = q.shape[-1]
+        Dk = kernel_head_dim(D)
+        q_, k_, v_ = (pad_head_dim(t.to(device=dev, dtype=torch.bfloat16, non_blocking=True), Dk)
+                      for t in (q, k, v))
+        o, lse = flash_attention_forward(q_, k_, v_, causal=causal, sm_scale=sm_scale)
+        ctx.save_for_backward(q_, k_, v_, o, lse)
+        ctx.causal, ctx.sm_scale, ctx.dev, ctx.D = causal, sm_scale, dev, D
+        o_h = _to_host(o[..., :D] if Dk != D else o)
+        lse_h = _to_host(lse)
+        torch.cuda.current_stream(dev).synchronize()
+        ctx.mark_non_differentiable(lse_h)
+        return o_h, lse_h
+
+    @staticmethod
+    def backward(ctx, do, _dlse):
+        q_, k_, v_, o, lse = ctx.saved_tensors
+        Dk = q_.shape[-1]
+        do_ = pad_head_dim(do.to(device=ctx.dev, dtype=torch.bfloat16, non_blocking=True), Dk)
+        dq, dk, dv = flash_attention_backward(q_, k_, v_, o, lse, do_, causal=ctx.causal,
+                                              sm_scale=ctx.sm_scale)
+        if Dk != ctx.D:
+            dq, dk, dv = (t[..., :ctx.D] for t in (dq, dk, dv))
+        out = tuple(_to_host(t) for t in (dq, dk, dv))
+        torch.cuda.current_stream(ctx.dev).synchronize()
+        return out + (None, None, None)
+
+
 def pallas_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                            causal: bool = False, sm_scale: Optional[float] = None,
                            return_lse: bool = False):
@@ -132,18 +176,17 @@ def pallas_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     """
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise ValueError("q, k, v must be [B, H, N, D]")
-    host = not q.is_cuda
-    dev = torch.device("cuda", torch.cuda.current_device()) if host else q.device
-    q_, k_, v_ = (t.to(device=dev, dtype=torch.bfloat16, non_blocking=True) for t in (q, k, v))
     D = q.shape[-1]
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
+    if not q.is_cuda:
+        dev = torch.device("cuda", torch.cuda.current_device())
+        o, lse = _HostFlashAttention.apply(q, k, v, bool(causal), float(sm_scale), dev)
+        return (o, lse) if return_lse else o
+    q_, k_, v_ = (t.to(dtype=torch.bfloat16) for t in (q, k, v))
     Dk = kernel_head_dim(D)
     q_, k_, v_ = (pad_head_dim(t, Dk) for t in (q_, k_, v_))
     o, lse = _FlashAttention.apply(q_, k_, v_, bool(causal), float(sm_scale))
     if Dk != D:
         o = o[..., :D]
-    if host:
-        o = o.to("cpu")
-        lse = lse.to("cpu")
     return (o, lse) if return_lse else o

@@ -123,3 +123,22 @@ def test_host_tensors_roundtrip(pf):
     assert out.device.type == "cpu"
     ro, _ = orc.mha_forward(to_np(q), to_np(q), to_np(q), causal=True)
     assert_close_o(to_np(out), ro)
+
+
+@pytest.mark.parametrize("D", [128, 80])
+def test_host_tensors_backward(pf, D):
+    """Host inputs with gradients: o and dq / dk / dv come back as pinned host
+    tensors equal to the ones the device path computes (same kernels)."""
+    shape = (1, 2, 384, D)
+    q, k, v = (randn(shape, 20 + i).requires_grad_() for i in range(3))
+    do = randn(shape, 30).pin_memory()
+    o = pf.pallas_flash_attention(q, k, v, causal=True)
+    assert o.device.type == "cpu" and o.is_pinned() and o.dtype == torch.bfloat16
+    o.backward(do)
+    assert all(t.grad is not None and t.grad.device.type == "cpu" for t in (q, k, v))
+    qd, kd, vd = (t.detach().cuda().requires_grad_() for t in (q, k, v))
+    od = pf.pallas_flash_attention(qd, kd, vd, causal=True)
+    od.backward(do.cuda())
+    assert torch.equal(o, od.cpu())
+    for h, d in ((q, qd), (k, kd), (v, vd)):
+        assert torch.equal(h.grad, d.grad.cpu())
