@@ -10,8 +10,9 @@ additions (defaults keep the reference's behaviour): `causal`,
 backward pass (which the reference lacks) reuses the saved LSE.
 
 Inputs may live on the GPU (the usual case) or on the host.  Host tensors are
-copied to the current CUDA device (asynchronously when they are pinned), and
-`o`, the LSE and, in the backward pass, dq / dk / dv come back as pinned host
+copied to the current CUDA device (asynchronously when they are pinned) in
+chunks of heads, pipelined with the kernels and with the copies back: `o`,
+the LSE and, in the backward pass, dq / dk / dv come back as pinned host
 tensors (one stream synchronisation per call).  Every compute step runs in
 libpu_attn.so (sm_100a); there is no CPU fallback.
 """
@@ -121,46 +122,93 @@ class _FlashAttention(torch.autograd.Function):
         return dq, dk, dv, None, None
 
 
-def _to_host(t: torch.Tensor) -> torch.Tensor:
-    """Asynchronous copy of a device tensor into a new pinned host tensor
-    (torch's pinned caching allocator reuses freed blocks)."""
-    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-    h.copy_(t, non_blocking=True)
-    return h
+_HOST_CHUNKS = 8   # pipeline depth of the host path over the B*H heads
+
+
+def _chunks(n: int, parts: int):
+    """[a, b) row ranges splitting n rows into at most `parts` nearly equal parts."""
+    parts = max(1, min(parts, n))
+    return [(i * n // parts, (i + 1) * n // parts) for i in range(parts)]
 
 
 class _HostFlashAttention(torch.autograd.Function):
-    """The attention of host tensors: inputs to the device, o / LSE and the
-    gradients back into pinned host memory.  The device copies of q, k, v, o
-    and the LSE are kept for the backward pass."""
+    """The attention of host tensors.  Heads are independent, so the B*H rows
+    are processed in chunks on three streams: the host-to-device copy of chunk
+    i+1, the kernels of chunk i and the device-to-host copy of chunk i-1 run
+    at the same time (PCIe carries both directions at once).  Results land in
+    pinned host tensors; the device copies of q, k, v, o and the LSE are kept
+    for the backward pass.  Every head's kernels are the same as unchunked,
+    so the results are identical."""
 
     @staticmethod
     def forward(ctx, q, k, v, causal, sm_scale, dev):
-        D = q.shape[-1]
+        B, H, Nq, D = q.shape
+        Nkv = k.shape[2]
         Dk = kernel_head_dim(D)
-        q_, k_, v_ = (pad_head_dim(t.to(device=dev, dtype=torch.bfloat16, non_blocking=True), Dk)
-                      for t in (q, k, v))
-        o, lse = flash_attention_forward(q_, k_, v_, causal=causal, sm_scale=sm_scale)
+        BH = B * H
+        main = torch.cuda.current_stream(dev)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        hq, hk, hv = (t.detach().reshape(BH, t.shape[2], D) for t in (q, k, v))
+        q_ = torch.zeros((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
+        k_ = torch.zeros((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
+        v_ = torch.zeros((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
+        o = torch.empty((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
+        lse = torch.empty((BH, Nq), dtype=torch.float32, device=dev)
+        o_h = torch.empty((BH, Nq, D), dtype=torch.bfloat16, pin_memory=True)
+        lse_h = torch.empty((BH, Nq), dtype=torch.float32, pin_memory=True)
+        s_in.wait_stream(main)             # the zero fills above
+        for a, b in _chunks(BH, _HOST_CHUNKS):
+            with torch.cuda.stream(s_in):
+                for h, d in ((hq, q_), (hk, k_), (hv, v_)):
+                    d[a:b, :, :D].copy_(h[a:b].to(dev, non_blocking=True))
+            main.wait_stream(s_in)
+            flash_attention_forward(q_[a:b].unsqueeze(0), k_[a:b].unsqueeze(0), v_[a:b].unsqueeze(0),
+                                    causal=causal, sm_scale=sm_scale, out=o[a:b].unsqueeze(0),
+                                    lse=lse[a:b].unsqueeze(0))
+            s_out.wait_stream(main)
+            with torch.cuda.stream(s_out):
+                o_h[a:b].copy_(o[a:b, :, :D], non_blocking=True)
+                lse_h[a:b].copy_(lse[a:b], non_blocking=True)
+        s_out.synchronize()
         ctx.save_for_backward(q_, k_, v_, o, lse)
-        ctx.causal, ctx.sm_scale, ctx.dev, ctx.D = causal, sm_scale, dev, D
-        o_h = _to_host(o[..., :D] if Dk != D else o)
-        lse_h = _to_host(lse)
-        torch.cuda.current_stream(dev).synchronize()
-        ctx.mark_non_differentiable(lse_h)
-        return o_h, lse_h
+        ctx.causal, ctx.sm_scale, ctx.dev, ctx.shape = causal, sm_scale, dev, (B, H, Nq, Nkv, D)
+        lse_out = lse_h.view(B, H, Nq)
+        ctx.mark_non_differentiable(lse_out)
+        return o_h.view(B, H, Nq, D), lse_out
 
     @staticmethod
     def backward(ctx, do, _dlse):
         q_, k_, v_, o, lse = ctx.saved_tensors
-        Dk = q_.shape[-1]
-        do_ = pad_head_dim(do.to(device=ctx.dev, dtype=torch.bfloat16, non_blocking=True), Dk)
-        dq, dk, dv = flash_attention_backward(q_, k_, v_, o, lse, do_, causal=ctx.causal,
-                                              sm_scale=ctx.sm_scale)
-        if Dk != ctx.D:
-            dq, dk, dv = (t[..., :ctx.D] for t in (dq, dk, dv))
-        out = tuple(_to_host(t) for t in (dq, dk, dv))
-        torch.cuda.current_stream(ctx.dev).synchronize()
-        return out + (None, None, None)
+        B, H, Nq, Nkv, D = ctx.shape
+        BH, Dk, dev = B * H, q_.shape[-1], ctx.dev
+        main = torch.cuda.current_stream(dev)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        hdo = do.detach().reshape(BH, Nq, D)
+        do_ = torch.zeros((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
+        dq = torch.empty((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
+        dk = torch.empty((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
+        dv = torch.empty((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
+        parts = _chunks(BH, _HOST_CHUNKS)
+        rows = max(b - a for a, b in parts)
+        ws = torch.empty(bwd_workspace_bytes(1, rows, Nq, Dk), dtype=torch.uint8, device=dev)
+        dq_h = torch.empty((BH, Nq, D), dtype=torch.bfloat16, pin_memory=True)
+        dk_h = torch.empty((BH, Nkv, D), dtype=torch.bfloat16, pin_memory=True)
+        dv_h = torch.empty((BH, Nkv, D), dtype=torch.bfloat16, pin_memory=True)
+        s_in.wait_stream(main)
+        for a, b in parts:
+            with torch.cuda.stream(s_in):
+                do_[a:b, :, :D].copy_(hdo[a:b].to(dev, non_blocking=True))
+            main.wait_stream(s_in)
+            c = lambda t: t[a:b].unsqueeze(0)   # noqa: E731
+            flash_attention_backward(c(q_), c(k_), c(v_), c(o), c(lse), c(do_), causal=ctx.causal,
+                                     sm_scale=ctx.sm_scale, workspace=ws, dq=c(dq), dk=c(dk), dv=c(dv))
+            s_out.wait_stream(main)
+            with torch.cuda.stream(s_out):
+                for d, h in ((dq, dq_h), (dk, dk_h), (dv, dv_h)):
+                    h[a:b].copy_(d[a:b, :, :D], non_blocking=True)
+        s_out.synchronize()
+        return (dq_h.view(B, H, Nq, D), dk_h.view(B, H, Nkv, D), dv_h.view(B, H, Nkv, D),
+                None, None, None)
 
 
 def pallas_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
