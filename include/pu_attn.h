@@ -165,6 +165,29 @@ PU_API int pu_decode_combine(const float* partials, int64_t G, void* o, float* l
                       int64_t B, int64_t H, int64_t D, void* stream);
 
 /*
+ * Library-owned NCCL communicator for the gather between pu_decode_partial
+ * and pu_decode_combine, for callers with no communicator of their own.
+ * Replaces the cross-device exchange of the reference's sharded decode: its
+ * psum/all_gather wrappers (src/pallas_flash/distributed/collectives.py:27-117)
+ * and the documented split-KV merge (README.md:41-46).  NCCL is loaded at
+ * first use (libnccl.so.2, the process's copy if one is loaded); without it
+ * these return PU_ERR_UNSUPPORTED.
+ *   pu_comm_unique_id: one rank creates the id (PU_COMM_ID_BYTES bytes) and
+ *     shares it with the others over any host channel.
+ *   pu_comm_init: every rank, with its own device current, joins; blocks
+ *     until all nranks ranks have joined.
+ *   pu_allgather_partials: partial fp32 [B*H][D+2] of this rank ->
+ *     gathered fp32 [nranks][B*H][D+2] on every rank (rank order), on stream.
+ *   pu_comm_destroy: after the last use on every rank.
+ */
+#define PU_COMM_ID_BYTES 128
+PU_API int pu_comm_unique_id(void* id);
+PU_API int pu_comm_init(const void* id, int64_t nranks, int64_t rank, void** comm);
+PU_API int pu_allgather_partials(const float* partial, float* gathered, int64_t B, int64_t H,
+                                 int64_t D, void* comm, void* stream);
+PU_API int pu_comm_destroy(void* comm);
+
+/*
  * Single-GPU decode step: pu_decode_partial over the whole cache with the
  * merge fused into the same kernel (the last CTA of each (b, h) combines).
  * Replaces pallas_flash_decoding (src/pallas_flash/kernels/decoding.py:105-145).

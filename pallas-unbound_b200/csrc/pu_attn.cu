@@ -9,6 +9,7 @@
 #include "outproj.cuh"
 #include "attn_fwd.cuh"
 #include "attn_bwd.cuh"
+#include "comm.cuh"
 
 // ---------------------------------------------------------------------------
 // Allocation-free decode step (pu_decode_noalloc).

@@ -23,6 +23,8 @@ PU_DTYPE_F16 = 1
 PU_DTYPE_F32 = 2
 PU_DTYPE_FP8_E4M3 = 3
 
+PU_COMM_ID_BYTES = 128
+
 _LIB_PATH = Path(__file__).resolve().parent / "_native" / "libpu_attn.so"
 
 _c_void_p = ctypes.c_void_p
@@ -80,6 +82,10 @@ SIGNATURES = {
     "pu_outproj_exchange_bytes": (_size_t, [_i64, _i64, _i64]),
     "pu_outproj_allreduce": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
                                     ctypes.c_uint32, _i64, _i64, _i64, ctypes.c_uint64, _c_void_p]),
+    "pu_comm_unique_id": (_int, [_c_void_p]),
+    "pu_comm_init": (_int, [_c_void_p, _i64, _i64, ctypes.POINTER(_c_void_p)]),
+    "pu_allgather_partials": (_int, [_c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p]),
+    "pu_comm_destroy": (_int, [_c_void_p]),
     "pu_kv_append": (_int, [_c_void_p, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p, _i64,
                             _i64, _i64, _c_void_p, _i64, _i64, _i64, _c_void_p]),
 }

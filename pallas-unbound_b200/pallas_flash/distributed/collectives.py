@@ -5,12 +5,18 @@ are XLA psum/all_gather wrappers that no kernel calls; its documented
 split-KV merge is a psum of LogSumExp terms (README.md:41-46).  Here the one
 real exchange step of the sequence-sharded decode is an NCCL all-gather of
 the packed fp32 (m, l, o) records over NVLink, through torch.distributed
-(backend "nccl" on GPUs, "gloo" in the CPU tests).
+(backend "nccl" on GPUs, "gloo" in the CPU tests), or through the library's
+own NCCL communicator (`LibComm`: pu_comm_* / pu_allgather_partials), the
+route a caller without torch.distributed (a C or JAX FFI runtime) takes.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
+
+from .. import _lib
 
 
 def all_gather_partials(part: torch.Tensor, world: int, group=None) -> torch.Tensor:
@@ -32,3 +38,57 @@ def sequence_shard(x: torch.Tensor, rank: int, world: int, axis: int = 2) -> tor
         raise ValueError(f"sequence length {n} is not divisible by {world} shards")
     step = n // world
     return x.narrow(axis, rank * step, step)
+
+
+class LibComm:
+    """The library's own NCCL communicator over the ranks of `group` (the
+    group only carries the unique id from rank 0 to the others).  One per
+    (group, device); `all_gather` runs pu_allgather_partials on the current
+    stream."""
+
+    def __init__(self, group=None):
+        g = group if group is not None else dist.group.WORLD
+        self.rank, self.world = dist.get_rank(g), dist.get_world_size(g)
+        lib = _lib.lib()
+        uid = (ctypes.c_uint8 * _lib.PU_COMM_ID_BYTES)()
+        if self.rank == 0:
+            _lib.check(lib.pu_comm_unique_id(uid), "pu_comm_unique_id")
+        box = [bytes(uid)]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(g, 0), group=g)
+        uid = (ctypes.c_uint8 * _lib.PU_COMM_ID_BYTES).from_buffer_copy(box[0])
+        self._comm = ctypes.c_void_p()
+        _lib.check(lib.pu_comm_init(uid, self.world, self.rank, ctypes.byref(self._comm)), "pu_comm_init")
+
+    def all_gather(self, part: torch.Tensor, B: int, H: int, D: int) -> torch.Tensor:
+        """fp32 [B*H, D+2] of this rank -> [world, B*H, D+2] on every rank."""
+        if part.dtype != torch.float32 or tuple(part.shape) != (B * H, D + 2) or not part.is_cuda:
+            raise TypeError(f"partial must be a CUDA fp32 [{B * H}, {D + 2}] tensor, got "
+                            f"{part.dtype} {tuple(part.shape)} on {part.device}")
+        part = part.contiguous()
+        out = torch.empty((self.world,) + tuple(part.shape), dtype=torch.float32, device=part.device)
+        _lib.check(_lib.lib().pu_allgather_partials(part.data_ptr(), out.data_ptr(), B, H, D, self._comm,
+                                                    torch.cuda.current_stream().cuda_stream),
+                   "pu_allgather_partials")
+        return out
+
+    def close(self):
+        if self._comm:
+            _lib.check(_lib.lib().pu_comm_destroy(self._comm), "pu_comm_destroy")
+            self._comm = ctypes.c_void_p()
+
+
+_COMMS: dict = {}
+
+
+def get_lib_comm(group=None) -> LibComm:
+    """The cached LibComm of (group, current device); built collectively on first use."""
+    key = (id(group), torch.cuda.current_device())
+    if key not in _COMMS:
+        _COMMS[key] = LibComm(group)
+    return _COMMS[key]
+
+
+def close_lib_comms():
+    for c in _COMMS.values():
+        c.close()
+    _COMMS.clear()

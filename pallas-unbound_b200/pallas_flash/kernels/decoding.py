@@ -20,7 +20,9 @@ Keyword-only additions:
               partials are all-gathered over NCCL, and a fused stable-LSE
               kernel merges them (the split-KV scheme the reference documents,
               README.md:41-46, but never implements).
-  transport   for a sharded cache: "nccl" (all-gather of the partials) or
+  transport   for a sharded cache: "nccl" (all-gather of the partials
+              through torch.distributed), "lib" (the same all-gather through
+              the library's own NCCL communicator, pu_allgather_partials) or
               "peer" (partials stored straight into every rank's exchange
               buffer over NVLink, flags instead of a collective; see
               distributed/peer.py)
@@ -177,14 +179,17 @@ def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch
             ws = DecodeWorkspace.get(dev, int(lib.pu_decode_workspace_size(B, H, n_local, D)))
             o, lse = ex.decode(q_, k_, v_, kv_offset=rank * n_local, kv_lens=lens,
                                sm_scale=sm_scale, workspace=ws)
-        elif transport == "nccl":
-            from ..distributed.collectives import all_gather_partials
+        elif transport in ("nccl", "lib"):
+            from ..distributed.collectives import all_gather_partials, get_lib_comm
             part = decode_partial(q_, k_, v_, kv_offset=rank * n_local, kv_lens=lens,
                                   sm_scale=sm_scale)
-            gathered = all_gather_partials(part, world, group)
+            if transport == "nccl":
+                gathered = all_gather_partials(part, world, group)
+            else:
+                gathered = get_lib_comm(group).all_gather(part, B, H, D)
             o, lse = decode_combine(gathered, B, H, D)
         else:
-            raise ValueError(f"unknown transport {transport!r} (nccl or peer)")
+            raise ValueError(f"unknown transport {transport!r} (nccl, lib or peer)")
     if host:
         o, lse = o.cpu(), lse.cpu()
     return (o, lse) if return_lse else o

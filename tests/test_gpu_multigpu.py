@@ -83,6 +83,18 @@ def _worker(rank, world, port, out_dir):
         same &= bool(torch.equal(o_n, o_p)) and bool(torch.equal(l_n, l_p))
     res["peer_equal"] = same
     res["peer_status"] = list(_lib.device_status())
+    # --- the same decode through the library's own NCCL communicator ---
+    from pallas_flash.distributed.collectives import close_lib_comms
+    same_lib = True
+    for step in range(3):
+        qs = randn((B, H, 1, D), 120 + step, dtype=torch.float16).cuda()
+        o_n, l_n = pallas_flash_decoding(qs, ks, vs, kv_lens=lens.cuda(), group=dist.group.WORLD,
+                                         return_lse=True)
+        o_l, l_l = pallas_flash_decoding(qs, ks, vs, kv_lens=lens.cuda(), group=dist.group.WORLD,
+                                         transport="lib", return_lse=True)
+        same_lib &= bool(torch.equal(o_n, o_l)) and bool(torch.equal(l_n, l_l))
+    close_lib_comms()
+    res["lib_equal"] = same_lib
     ex = peer.get_exchange(B, H, D, dist.group.WORLD)
     o_t = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device="cuda")
     # an epoch no rank will publish: the wait must run out (50 ms) and report
@@ -146,6 +158,7 @@ def test_two_gpu_decode_and_partitioned_training(tmp_path, built_lib):
         assert res["dec_o"]["max_abs"] <= 2e-2 and res["dec_o"]["rel"] <= 1e-2, res
         assert res["dec_lse"]["max_abs"] <= 1e-3, res
         assert res["peer_equal"] and res["peer_status"] == [0, 0], res
+        assert res["lib_equal"], res
         assert res["timeout_status"] == [5, 304], res
         assert res["after_timeout"]["max_abs"] <= 2e-2 and res["after_timeout"]["rel"] <= 1e-2, res
         assert res["outproj_same"] and res["outproj_err"] <= 1e-2 and res["outproj_status"] == [0, 0], res

@@ -56,3 +56,17 @@ def test_argument_errors_are_reported_without_gpu(built_lib):
     assert b"null" in lib.pu_last_error()
     rc = lib.pu_decode_combine(None, 1, None, None, 1, 1, 128, None)
     assert rc == _lib.PU_ERR_INVALID_ARGUMENT
+
+
+def test_comm_argument_errors_without_gpu(built_lib):
+    """The communicator entry points check their arguments before touching
+    NCCL or the GPU; destroying a null communicator is a no-op."""
+    import ctypes as ct
+    from pallas_flash import _lib
+    lib = _lib.lib()
+    comm = ct.c_void_p()
+    assert lib.pu_comm_init(None, 1, 0, ct.byref(comm)) == _lib.PU_ERR_INVALID_ARGUMENT
+    uid = (ct.c_uint8 * _lib.PU_COMM_ID_BYTES)()
+    assert lib.pu_comm_init(uid, 2, 2, ct.byref(comm)) == _lib.PU_ERR_INVALID_ARGUMENT
+    assert lib.pu_allgather_partials(None, None, 1, 1, 128, None, None) == _lib.PU_ERR_INVALID_ARGUMENT
+    assert lib.pu_comm_destroy(None) == _lib.PU_OK
