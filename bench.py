@@ -641,7 +641,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["pu", "reference"], default="pu")
     ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--profile-leg", choices=["attn", "decode", "gqa"], default=None,
+    ap.add_argument("--profile-leg", choices=["attn", "decode", "gqa", "outproj"], default=None,
                     help="run only this leg and print no JSON (small runs for ncu captures)")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
@@ -659,6 +659,10 @@ def main():
     if args.profile_leg == "gqa":
         us = profile_gqa(args.steps, warmup)
         print(f"grouped-head decode leg: {us:.1f} us/step", flush=True)
+        return
+    if args.profile_leg == "outproj":
+        op = bench_outproj(args.steps, warmup, rank, world)
+        print(f"out-projection leg: {op['peer']:.1f} us/step", flush=True)
         return
     clocks = ClockSampler(local).start()
     total_ms, fwd_ms, bwd_ms = bench_attention(args.steps, warmup, rank, world, clocks)
