@@ -125,6 +125,17 @@ class _FlashAttention(torch.autograd.Function):
 _HOST_CHUNKS = 8   # pipeline depth of the host path over the B*H heads
 
 
+_COPY_STREAMS: dict = {}
+
+
+def _copy_streams(dev: torch.device):
+    """The (copy-in, copy-out) streams of `dev`, created once per device."""
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    if key not in _COPY_STREAMS:
+        _COPY_STREAMS[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _COPY_STREAMS[key]
+
+
 def _chunks(n: int, parts: int):
     """[a, b) row ranges splitting n rows into at most `parts` nearly equal parts."""
     parts = max(1, min(parts, n))
@@ -147,7 +158,7 @@ class _HostFlashAttention(torch.autograd.Function):
         Dk = kernel_head_dim(D)
         BH = B * H
         main = torch.cuda.current_stream(dev)
-        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        s_in, s_out = _copy_streams(dev)
         hq, hk, hv = (t.detach().reshape(BH, t.shape[2], D) for t in (q, k, v))
         q_ = torch.zeros((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
         k_ = torch.zeros((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
@@ -182,7 +193,7 @@ class _HostFlashAttention(torch.autograd.Function):
         B, H, Nq, Nkv, D = ctx.shape
         BH, Dk, dev = B * H, q_.shape[-1], ctx.dev
         main = torch.cuda.current_stream(dev)
-        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        s_in, s_out = _copy_streams(dev)
         hdo = do.detach().reshape(BH, Nq, D)
         do_ = torch.zeros((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
         dq = torch.empty((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
