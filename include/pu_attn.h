@@ -62,6 +62,14 @@ extern "C" {
  */
 PU_API const char* pu_version(void);
 
+/*
+ * Architecture of the machine code the current device would run for this
+ * library's kernels (cudaFuncGetAttributes binaryVersion of every kernel,
+ * major*10 + minor; 100 for sm_100a), written to *arch.  Returns an error if
+ * the kernels disagree or cannot be loaded.  No reference counterpart.
+ */
+PU_API int pu_binary_arch(int* arch);
+
 /* Message for the last error raised on the calling thread ("" if none). */
 PU_API const char* pu_last_error(void);
 
@@ -101,8 +109,9 @@ PU_API int pu_attn_fwd(const void* q, const void* k, const void* v, void* o, flo
                 float sm_scale, int causal, void* stream);
 
 /*
- * Bytes of device workspace pu_attn_bwd needs (an fp32 dQ accumulator and
- * the row statistics Delta = rowsum(dO*O)).
+ * Bytes of device workspace pu_attn_bwd (and pu_attn_bwd_deterministic)
+ * needs: the row statistics LSE*log2(e) and Delta = rowsum(dO*O), and for
+ * D = 128 an fp32 dQ accumulator [B*H][Nq rounded up to 128][D].
  */
 PU_API size_t pu_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t Nq, int64_t D);
 
@@ -112,8 +121,28 @@ PU_API size_t pu_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t Nq, int64
  * replaces the autodiff of benchmarks/baseline_mha.py:22-58.
  *   workspace: >= pu_attn_bwd_workspace_size() bytes, 256-byte aligned;
  *   its contents need not be initialised.
+ * For D = 128 one fused pass computes all five products of every (key
+ * tile, query tile) pair and adds dQ into the fp32 accumulator with
+ * reductions in L2, so dQ's last bits depend on the order in which key
+ * tiles finish (dK and dV are deterministic); D = 64 runs the two-kernel
+ * path of pu_attn_bwd_deterministic.
  */
 PU_API int pu_attn_bwd(const void* q, const void* k, const void* v, const void* o,
+                const float* lse, const void* dout,
+                void* dq, void* dk, void* dv,
+                void* workspace, size_t workspace_bytes,
+                int64_t B, int64_t H, int64_t Nq, int64_t Nkv, int64_t D,
+                float sm_scale, int causal, void* stream);
+
+/*
+ * The same gradients, bitwise reproducible run to run (same replacement of
+ * the autodiff of benchmarks/baseline_mha.py:22-58): a dK/dV kernel per key
+ * tile and a dQ kernel per query tile, each gradient element written once
+ * with no atomics.  S and dP are computed in both kernels, so it performs 7
+ * of the 128x128xD products per tile pair instead of 5 and is slower.
+ * Same arguments and workspace as pu_attn_bwd.
+ */
+PU_API int pu_attn_bwd_deterministic(const void* q, const void* k, const void* v, const void* o,
                 const float* lse, const void* dout,
                 void* dq, void* dk, void* dv,
                 void* workspace, size_t workspace_bytes,

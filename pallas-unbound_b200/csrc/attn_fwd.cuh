@@ -440,16 +440,9 @@ int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   if (!rc) rc = make_tmap_bf16_3d(&tk, k, D, Nkv, B * H, 64, BN, true);
   if (!rc) rc = make_tmap_bf16_3d(&tv, v, D, Nkv, B * H, 64, BN, true);
   if (rc) return rc;
-  static bool attr_done[64] = {false};
-  const int dev = current_device();
-  if (dev < 0) return PU_ERR_CUDA;
-  if (dev >= 64 || !attr_done[dev]) {
-    rc = check_cuda(cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes),
-                    "cudaFuncSetAttribute(fwd smem)");
-    if (rc) return rc;
-    if (dev < 64) attr_done[dev] = true;
-  }
+  rc = set_max_dynamic_smem(reinterpret_cast<const void*>(attn_fwd_kernel<D>), C::kSmemBytes,
+                            "cudaFuncSetAttribute(fwd smem)");
+  if (rc) return rc;
   Params prm{};
   prm.Nq = (int)Nq;
   prm.Nkv = (int)Nkv;

@@ -6,6 +6,8 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "pu_host.cuh"
 #include "pu_ptx.cuh"
@@ -98,6 +100,19 @@ int current_device() {
     return -1;
   }
   return dev;
+}
+
+int set_max_dynamic_smem(const void* func, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  const int dev = current_device();
+  if (dev < 0) return PU_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({func, dev})) return PU_OK;
+  const int rc =
+      check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+  if (!rc) done.insert({func, dev});
+  return rc;
 }
 
 int sm_count() {

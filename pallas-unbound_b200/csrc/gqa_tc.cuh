@@ -523,13 +523,9 @@ inline Plan tc_plan(long long B, long long H, long long H_kv, long long n, int n
 template <typename T, int NP>
 int launch_np(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, dim3 grid, cudaStream_t st) {
   constexpr int smem = Cfg<NP>::kSmemBytes;
-  static bool configured = false;   // per instantiation; the attribute is per function
-  if (!configured) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(gqa_tc_kernel<T, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return check_cuda(e, "grouped-head decode (tensor core) shared memory");
-    configured = true;
-  }
+  const int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(gqa_tc_kernel<T, NP>), smem,
+                                      "grouped-head decode (tensor core) shared memory");
+  if (rc) return rc;
   gqa_tc_kernel<T, NP><<<grid, kThreads, smem, st>>>(tk, tv, prm);
   return check_cuda(cudaGetLastError(), "grouped-head decode (tensor core) launch");
 }

@@ -410,15 +410,9 @@ int pu_outproj_allreduce(const void* o_local, const void* w_local, void* y, void
   rc = pu::make_tmap_bf16_3d(&tmW, w_local, (uint64_t)N, (uint64_t)K, 1, 64, BK, true);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  static bool attr_set[64] = {false};
-  const int dev = pu::current_device();
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    rc = pu::check_cuda(cudaFuncSetAttribute(outproj_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSmemBytes),
-                        "outproj smem attribute");
-    if (rc) return rc;
-    attr_set[dev] = true;
-  }
+  rc = pu::set_max_dynamic_smem(reinterpret_cast<const void*>(outproj_gemm_kernel), kSmemBytes,
+                                "outproj smem attribute");
+  if (rc) return rc;
   outproj_gemm_kernel<<<std::min(l.n_tiles, pu::sm_count()), kThreads, kSmemBytes, st>>>(tmO, tmW, prm);
   rc = pu::check_cuda(cudaGetLastError(), "outproj GEMM launch");
   if (rc || G == 1) return rc;                        // one rank: the GEMM wrote y

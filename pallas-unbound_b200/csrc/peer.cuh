@@ -42,7 +42,11 @@ int pu_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle) {
   void* p = nullptr;
   int rc = pu::check_cuda(cudaMalloc(&p, bytes), "cudaMalloc (exchange buffer)");
   if (rc) return rc;
+  // cudaMemset of device memory may return before the zeros land; finish it
+  // here so a peer that opens the handle can never have its first records
+  // erased by a zeroing still in flight
   rc = pu::check_cuda(cudaMemset(p, 0, bytes), "cudaMemset (exchange buffer)");
+  if (!rc) rc = pu::check_cuda(cudaDeviceSynchronize(), "synchronize after zeroing the exchange buffer");
   if (!rc) {
     cudaIpcMemHandle_t h;
     rc = pu::check_cuda(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");

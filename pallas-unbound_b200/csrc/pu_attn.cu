@@ -93,3 +93,26 @@ extern "C" int pu_decode_noalloc(const void* q, int q_dtype, const void* k_cache
   prm.lse = lse;
   return launch<true>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), st);
 }
+
+// Binary architecture of the loaded kernels (one of each family).
+extern "C" int pu_binary_arch(int* arch) {
+  if (!arch) return pu::set_error(PU_ERR_INVALID_ARGUMENT, "null arch");
+  const void* kernels[] = {
+      reinterpret_cast<const void*>(pu::fwd::attn_fwd_kernel<128>),
+      reinterpret_cast<const void*>(pu::bwd::attn_bwd_fused_kernel),
+      reinterpret_cast<const void*>(pu::bwd::attn_bwd_dkdv_kernel<128>),
+      reinterpret_cast<const void*>(pu::outproj::outproj_gemm_kernel),
+  };
+  int seen = -1;
+  for (const void* k : kernels) {
+    cudaFuncAttributes a{};
+    const int rc = pu::check_cuda(cudaFuncGetAttributes(&a, k), "cudaFuncGetAttributes");
+    if (rc) return rc;
+    if (seen >= 0 && a.binaryVersion != seen)
+      return pu::set_error(PU_ERR_UNSUPPORTED, "kernels built for different architectures (%d, %d)", seen,
+                           a.binaryVersion);
+    seen = a.binaryVersion;
+  }
+  *arch = seen;
+  return PU_OK;
+}

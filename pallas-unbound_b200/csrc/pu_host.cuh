@@ -29,6 +29,10 @@ int sm_count();
 // Current device ordinal (or -1 with the error set).
 int current_device();
 
+// Raise `func`'s dynamic shared-memory limit to `bytes` on the current device,
+// once per (kernel, device); thread-safe.  Returns PU_OK or an error code.
+int set_max_dynamic_smem(const void* func, int bytes, const char* what);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace pu

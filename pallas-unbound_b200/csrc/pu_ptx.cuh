@@ -218,15 +218,6 @@ __device__ __forceinline__ void tma_store_3d(const void* desc, const void* smem_
       : "memory");
 }
 
-// smem -> global elementwise fp32 add (tile mode), used for dQ accumulation.
-__device__ __forceinline__ void tma_reduce_add_3d(const void* desc, const void* smem_src, int c0,
-                                                  int c1, int c2) {
-  asm volatile(
-      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(desc)),
-      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -38,6 +38,7 @@ SIGNATURES = {
     "pu_version": (ctypes.c_char_p, []),
     "pu_last_error": (ctypes.c_char_p, []),
     "pu_device_status": (_int, [ctypes.POINTER(_int)]),
+    "pu_binary_arch": (_int, [ctypes.POINTER(_int)]),
     "pu_selftest_wait_timeout": (_int, [ctypes.c_uint64, _c_void_p]),
     "pu_attn_fwd": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                            _i64, _i64, _i64, _i64, _i64, _float, _int, _c_void_p]),
@@ -45,6 +46,10 @@ SIGNATURES = {
     "pu_attn_bwd": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                            _c_void_p, _c_void_p, _c_void_p, _c_void_p, _size_t,
                            _i64, _i64, _i64, _i64, _i64, _float, _int, _c_void_p]),
+    "pu_attn_bwd_deterministic": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                         _size_t, _i64, _i64, _i64, _i64, _i64, _float, _int,
+                                         _c_void_p]),
     "pu_decode_workspace_size": (_size_t, [_i64, _i64, _i64, _i64]),
     "pu_decode_partial": (_int, [_c_void_p, _int, _c_void_p, _c_void_p, _int, _c_void_p, _i64,
                                  _c_void_p, _c_void_p, _size_t, _i64, _i64, _i64, _i64, _float,

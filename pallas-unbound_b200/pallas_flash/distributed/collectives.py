@@ -40,6 +40,56 @@ def sequence_shard(x: torch.Tensor, rank: int, world: int, axis: int = 2) -> tor
     return x.narrow(axis, rank * step, step)
 
 
+def length_balanced_split(lens, world: int, granule: int = 128):
+    """Sequence sharding by held tokens: rank r takes a contiguous slice of
+    every sequence b, of about lens[b] / world tokens, so each rank reads the
+    same number of K/V bytes however ragged the batch is (contiguous chunks of
+    the padded capacity leave the high ranks idle past every sequence's end).
+
+    Slices are whole `granule`-token blocks except the last block of a
+    sequence; the blocks left over by the integer split go to the ranks
+    (r - b) mod world < remainder, so the extra blocks rotate over ranks and
+    no rank collects one from every sequence.
+
+    Returns (starts, counts): int64 arrays [world, B]; rank r holds tokens
+    [starts[r, b], starts[r, b] + counts[r, b]) of sequence b.
+    """
+    import numpy as np
+    lens = np.asarray(lens, dtype=np.int64).reshape(-1)
+    if world < 1 or granule < 1 or (lens < 0).any():
+        raise ValueError("world and granule must be positive, lengths non-negative")
+    B = lens.shape[0]
+    blocks = (lens + granule - 1) // granule
+    base, rem = blocks // world, blocks % world
+    r = np.arange(world)[:, None]
+    b = np.arange(B)[None, :]
+    nblk = base[None, :] + (((r - b) % world) < rem[None, :]).astype(np.int64)
+    first = np.concatenate([np.zeros((1, B), dtype=np.int64), np.cumsum(nblk, axis=0)[:-1]], axis=0)
+    starts = np.minimum(first * granule, lens[None, :])
+    ends = np.minimum((first + nblk) * granule, lens[None, :])
+    return starts, ends - starts
+
+
+def shard_by_length(k_cache: torch.Tensor, v_cache: torch.Tensor, lens, rank: int, world: int,
+                    granule: int = 128, capacity: int | None = None):
+    """This rank's length-balanced shard of full caches [B, H, N, D]: local
+    caches [B, H, capacity, D] holding its slice of every sequence from row 0
+    (rows past the slice are zero), and the local lengths int32 [B].
+    `capacity` defaults to the longest local slice rounded up to `granule`."""
+    starts, counts = length_balanced_split(lens, world, granule)
+    st, ct = starts[rank], counts[rank]
+    cap = capacity if capacity is not None else max(granule, int(-(-int(ct.max()) // granule) * granule))
+    B, H, _, D = k_cache.shape
+    kl = torch.zeros((B, H, cap, D), dtype=k_cache.dtype, device=k_cache.device)
+    vl = torch.zeros_like(kl)
+    for b in range(B):
+        n = int(ct[b])
+        if n:
+            kl[b, :, :n] = k_cache[b, :, int(st[b]):int(st[b]) + n]
+            vl[b, :, :n] = v_cache[b, :, int(st[b]):int(st[b]) + n]
+    return kl, vl, torch.as_tensor(ct, dtype=torch.int32)
+
+
 class LibComm:
     """The library's own NCCL communicator over the ranks of `group` (the
     group only carries the unique id from rank 0 to the others).  One per

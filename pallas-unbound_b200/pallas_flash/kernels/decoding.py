@@ -20,6 +20,13 @@ Keyword-only additions:
               partials are all-gathered over NCCL, and a fused stable-LSE
               kernel merges them (the split-KV scheme the reference documents,
               README.md:41-46, but never implements).
+  sharding    for a sharded cache: "contiguous" (rank r holds positions
+              [r*N_local, (r+1)*N_local) of every sequence; kv_lens are the
+              global lengths) or "by_length" (rank r holds its slice of every
+              sequence's held tokens from row 0 of its local cache, as
+              distributed.collectives.length_balanced_split assigns them;
+              kv_lens are this rank's local lengths), so a ragged batch keeps
+              every rank equally busy
   transport   for a sharded cache: "nccl" (all-gather of the partials
               through torch.distributed), "lib" (the same all-gather through
               the library's own NCCL communicator, pu_allgather_partials) or
@@ -114,7 +121,7 @@ def decode_combine(parts: torch.Tensor, B: int, H: int, D: int, *, out=None, lse
 def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
                           kv_lens: Optional[torch.Tensor] = None,
                           sm_scale: Optional[float] = None, return_lse: bool = False,
-                          group=None, transport: str = "nccl",
+                          group=None, transport: str = "nccl", sharding: str = "contiguous",
                           page_table: Optional[torch.Tensor] = None,
                           k_scale: float = 1.0, v_scale: float = 1.0):
     """One decode step of attention for a query token per (b, h)."""
@@ -173,15 +180,23 @@ def pallas_flash_decoding(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch
         import torch.distributed as dist
         rank = dist.get_rank(group)
         world = dist.get_world_size(group)
+        if sharding == "contiguous":
+            kv_offset = rank * n_local
+        elif sharding == "by_length":
+            if lens is None:
+                raise ValueError('sharding="by_length" needs this rank\'s kv_lens')
+            kv_offset = 0
+        else:
+            raise ValueError(f"unknown sharding {sharding!r} (contiguous or by_length)")
         if transport == "peer":
             from ..distributed.peer import get_exchange
             ex = get_exchange(B, H, D, group)
             ws = DecodeWorkspace.get(dev, int(lib.pu_decode_workspace_size(B, H, n_local, D)))
-            o, lse = ex.decode(q_, k_, v_, kv_offset=rank * n_local, kv_lens=lens,
+            o, lse = ex.decode(q_, k_, v_, kv_offset=kv_offset, kv_lens=lens,
                                sm_scale=sm_scale, workspace=ws)
         elif transport in ("nccl", "lib"):
             from ..distributed.collectives import all_gather_partials, get_lib_comm
-            part = decode_partial(q_, k_, v_, kv_offset=rank * n_local, kv_lens=lens,
+            part = decode_partial(q_, k_, v_, kv_offset=kv_offset, kv_lens=lens,
                                   sm_scale=sm_scale)
             if transport == "nccl":
                 gathered = all_gather_partials(part, world, group)

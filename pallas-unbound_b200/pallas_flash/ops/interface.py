@@ -78,8 +78,13 @@ def flash_attention_backward(q, k, v, o, lse, do, *, causal: bool = False,
                              workspace: Optional[torch.Tensor] = None,
                              dq: Optional[torch.Tensor] = None,
                              dk: Optional[torch.Tensor] = None,
-                             dv: Optional[torch.Tensor] = None):
-    """Low-level backward on CUDA bf16 tensors; returns (dq, dk, dv) bf16."""
+                             dv: Optional[torch.Tensor] = None,
+                             deterministic: bool = False):
+    """Low-level backward on CUDA bf16 tensors; returns (dq, dk, dv) bf16.
+
+    `deterministic=True` selects pu_attn_bwd_deterministic (bitwise
+    reproducible dQ, slower); the default pu_attn_bwd reduces dQ in fp32
+    through L2, so its last bits may vary from run to run."""
     for name, t in (("q", q), ("k", k), ("v", v), ("o", o), ("do", do)):
         _require_cuda(t, name)
         if t.dtype != torch.bfloat16:
@@ -96,11 +101,12 @@ def flash_attention_backward(q, k, v, o, lse, do, *, causal: bool = False,
     dq = torch.empty_like(q) if dq is None else dq
     dk = torch.empty_like(k) if dk is None else dk
     dv = torch.empty_like(v) if dv is None else dv
-    _lib.check(_lib.lib().pu_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                                      lse.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                                      dv.data_ptr(), workspace.data_ptr(), need, B, H, Nq, Nkv, D,
-                                      float(sm_scale), int(bool(causal)), _stream_handle()),
-               "pu_attn_bwd")
+    name = "pu_attn_bwd_deterministic" if deterministic else "pu_attn_bwd"
+    _lib.check(getattr(_lib.lib(), name)(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                         lse.data_ptr(), do.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                         dv.data_ptr(), workspace.data_ptr(), need, B, H, Nq, Nkv, D,
+                                         float(sm_scale), int(bool(causal)), _stream_handle()),
+               name)
     return dq, dk, dv
 
 

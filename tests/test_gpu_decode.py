@@ -82,6 +82,25 @@ def test_decode_sharded_combine(dec, G):
     assert_close_lse(to_np(lse), rl)
 
 
+@pytest.mark.parametrize("G", [2, 4, 8])
+def test_decode_length_balanced_shards(dec, G):
+    """Length-balanced shards (every rank a slice of every sequence's held
+    tokens, read with local lengths and no offset), one partial per shard,
+    stable combine == the whole ragged cache."""
+    from pallas_flash.distributed import collectives
+    B, H, N, D = 4, 4, 6144, 128
+    q, k, v = _inputs(B, H, N, D, 15)
+    lens = np.array([6144, 4097, 128, 1])
+    parts = []
+    for r in range(G):
+        kl, vl, ll = collectives.shard_by_length(k, v, lens, r, G, granule=128)
+        parts.append(dec.decode_partial(q.cuda(), kl.cuda(), vl.cuda(), kv_offset=0, kv_lens=ll.cuda()))
+    o, lse = dec.decode_combine(torch.stack(parts), B, H, D)
+    ro, rl = orc.decode_forward(to_np(q), to_np(k), to_np(v), kv_lens=lens)
+    assert_close_o(to_np(o), ro)
+    assert_close_lse(to_np(lse), rl)
+
+
 def test_decode_c4_full_size(dec):
     """B=1 H=32, 32768-token fp16 cache, D=128 (the split-KV decode benchmark shape)."""
     B, H, N, D = 1, 32, 32768, 128

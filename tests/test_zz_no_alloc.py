@@ -5,9 +5,11 @@ handler that only receives its operands and results, or a runtime that plans
 all device memory up front and forbids later allocation).  For them the
 library keeps a fixed 8 MiB scratch array in its own device memory.  These
 tests call the entry point through the C ABI (ctypes) and check that two
-calls in a row give what the workspace-taking pu_decode gives, within the
-bf16 output tolerance used by the other decode tests, and that problems too
-large for the fixed scratch are refused before anything runs.
+calls in a row give what the workspace-taking pu_decode gives and what the
+CPU oracle's decode (oracle/attention.py, the restatement of the
+reference's decode step) gives, within the bf16 output tolerance used by the
+other decode tests, and that problems too large for the fixed scratch are
+refused before anything runs.
 
 This file is collected last on purpose, and it passes both on its own in a
 fresh process and after the rest of the suite.
@@ -20,6 +22,7 @@ import pytest
 import torch
 
 from helpers import assert_close_lse, assert_close_o, randn, to_np
+from oracle import attention as orc
 
 pytestmark = pytest.mark.gpu
 
@@ -69,12 +72,16 @@ def test_no_alloc_matches_workspace_entry_point(lib, B, H, n, ragged):
     if ragged:
         lens = torch.tensor([n, 1, n // 3][:B], dtype=torch.int32, device="cuda")
     ref_o, ref_lse = _with_workspace(lib, q, k, v, lens)
+    orc_o, orc_lse = orc.decode_forward(to_np(q), to_np(k), to_np(v),
+                                        kv_lens=None if lens is None else lens.cpu().numpy())
     for _ in range(2):  # two calls in a row share (and must re-clear) the static scratch
         o, lse = _no_alloc(lib, q, k, v, lens)
         torch.cuda.synchronize()
         assert lib.device_status()[0] == 0
         assert_close_o(to_np(o), to_np(ref_o))
         assert_close_lse(to_np(lse), to_np(ref_lse))
+        assert_close_o(to_np(o), orc_o, what="o vs oracle")
+        assert_close_lse(to_np(lse).reshape(orc_lse.shape), orc_lse)
 
 
 def test_no_alloc_rejects_problems_beyond_the_scratch(lib):
