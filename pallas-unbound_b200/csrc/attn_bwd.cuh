@@ -662,11 +662,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 //                                    from shared memory; lanes = head dim)
 // dQ^T reuses dP^T's columns once the compute warps have read dP^T and
 // written dS^T; four drain warps (one per TMEM lane quarter, thread = one
-// head-dim column d) read it and add it to dq_acc[q][d] with coalesced
+// head-dim column d) add it to dq_acc[q][d] with coalesced
 // `red.global.add.f32` (a warp covers 32 consecutive d of one query row, one
-// 128-byte line per instruction), then release the columns for the next
-// dP^T.  Tensor order per query tile i:
+// 128-byte line per instruction): the first 64 query columns, then the other
+// 64 read, the columns released for the next dP^T, and those 64 added.
+// Tensor order per query tile i:
 //   dV_i, S_{i+1}, dK_i, dQ_i, [dQ_i drained] dP_{i+1}.
+// Measured limits of this arrangement (clock64 traces of one CTA, causal
+// B4 H16 N4096): ~6k SM cycles per tile pair against 2.6k of tensor work.
+// The 64 KB of dQ reductions per tile pair move at about 20 bytes per SM
+// clock whether issued as per-thread reductions or as TMA bulk reduce-adds,
+// and the per-thread form slows the compute warps' shared-memory traffic;
+// 64-row query tiles (which would give dQ^T its own TMEM columns) need N = 64
+// products, which cost as much per instruction as N = 128 ones.
 // Warps: 0-7 compute (two warpgroups, 64 query columns each), 8-11 dQ drain,
 // 12 TMA producer, 13 tcgen05 issuer / TMEM owner.
 // CTAs walk groups of kHeadGroup heads (so one group's dq_acc, Q and dO stay
@@ -892,18 +900,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if (!ok) break;
       tc_fence_after();
       float* rowp = acc_bh + (size_t)q0 * D;
-      // all 128 columns into registers first, so dP^T of the next query
-      // tile can be issued before the reductions drain through L2
-      uint32_t v[128];
+      uint32_t v[64];
+      tmem_ld64(tmem + lane_base + C::kColDP, v);
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld32(tmem + lane_base + C::kColDP + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
-      tmem_wait_ld();
-      reg_fence(v);
+      for (int c = 0; c < 64; ++c) red_add_f32(rowp + (size_t)c * D, __uint_as_float(v[c]));
+      tmem_ld64(tmem + lane_base + C::kColDP + 64, v);
       tc_fence_before();
       mbar_arrive(bDQd);
 #pragma unroll
-      for (int c = 0; c < 128; ++c) red_add_f32(rowp + (size_t)c * D, __uint_as_float(v[c]));
+      for (int c = 0; c < 64; ++c) red_add_f32(rowp + (size_t)(64 + c) * D, __uint_as_float(v[c]));
     }
   } else {
     // ---------------- compute warpgroups (warps 0-3: query cols 0-63, 4-7: 64-127) ----------------

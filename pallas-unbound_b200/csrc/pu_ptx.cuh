@@ -218,6 +218,15 @@ __device__ __forceinline__ void tma_store_3d(const void* desc, const void* smem_
       : "memory");
 }
 
+// shared -> global elementwise fp32 add of `bytes` contiguous bytes (16-byte
+// aligned addresses, size a multiple of 16), tracked by the bulk groups.
+__device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(gdst)),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
