@@ -15,6 +15,12 @@ The same line carries the split-KV decode measurement (B=1, H=32, a
 32768-token fp16 KV cache sharded by sequence over the N GPUs, NCCL
 all-gather of the (m, l, o) partials, fused LSE combine) as `decode`.
 
+Before any timed leg every rank checks small seeded cases of each path it
+runs against the oracle (head-partitioned causal fwd+bwd, the
+sequence-sharded decode over each transport, the length-balanced ragged
+decode, the fused out-projection) and the line carries the worst errors over
+the ranks as `parity`; a miss makes the run exit non-zero after printing.
+
 `--impl reference` times the reference algorithm on the host CPU instead
 (the numpy restatement in oracle/, since the JAX reference cannot run
 here) on a bounded sample of the same workload.
@@ -41,15 +47,19 @@ DEC_B, DEC_H, DEC_N, DEC_D = 1, 32, 32768, 128
 FWD_FLOPS = 4 * B * H * N * N * D * 0.5          # causal
 STEP_FLOPS = FWD_FLOPS * 3.5                      # fwd + 2.5x bwd
 L2_BYTES = 126 * 1024 * 1024
-# DRAM bytes (read + write) per launch from one ncu capture of this workload
-# (see the summaries under profiles/); re-measured whenever a kernel changes.
+# DRAM bytes (read + write) per launch of this workload, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum) of
+# `python bench.py --profile-leg attn --steps 2 --warmup 3` on one B200, the
+# command and date in TRAFFIC_CAPTURE; re-captured whenever a kernel changes.
 NCU_TRAFFIC_BYTES = {
-    "attn_fwd": 543_731_968 + 50_730_752,
-    # dK/dV + dQ measured; prep (reads O and dO, writes the row statistics) counted at
-    # its algorithmic 135 MB
-    "attn_bwd": (936_651_008 + 105_057_536) + (964_845_056 + 51_491_328) + 135_000_000,
+    "attn_fwd": 523_139_584 + 49_843_712,
+    # prep (135.3 + 84.0 MB) + fused backward (404.8 + 218.1 MB) + dQ conversion (134.2 + 32.5 MB)
+    "attn_bwd": (135_290_368 + 83_952_384) + (404_835_840 + 218_139_136) + (134_240_000 + 32_545_792),
     "split_kv": 536_904_192 + 3_470_848,
 }
+TRAFFIC_CAPTURE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none "
+                   "-k regex:'attn_fwd|prep_kernel|attn_bwd_fused|dq_convert' -s 12 -c 4 "
+                   "python bench.py --profile-leg attn --steps 2 --warmup 3 (2026-12-02)")
 
 
 def load_peaks() -> dict:
@@ -223,6 +233,133 @@ def cpu_decode_sample(heads: int = 8):
 
 
 # ---------------------------------------------------------------------------
+# Parity of every measured path on small seeded cases (the oracle is the
+# checker; nothing here is timed)
+# ---------------------------------------------------------------------------
+PARITY_TOL = {"o_max_abs": 2e-2, "o_rel": 1e-2, "lse_abs": 1e-3, "grad_rel": 3e-2}
+
+
+def single_rank_group():
+    """A one-rank gloo group (the peer-memory entry points take a group even
+    when there is nothing to exchange)."""
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:" + str(_free_port()),
+                                rank=0, world_size=1)
+    return dist.group.WORLD
+
+
+def run_parity(rank: int, world: int) -> dict:
+    """Small seeded cases of each path against the oracle on every rank;
+    returns {case: {max_abs, rel, ok}} with the worst value over the ranks.
+
+    * attn_fwd_bwd: causal B=1, 2 heads per rank (heads partitioned as in the
+      timed leg), N=384, D=128; O and LSE, then dQ/dK/dV.
+    * decode_<transport>: B=1 H=8, 1024 cache tokens per rank (sequence
+      shards of one 1024*world-token fp16 cache) over each transport.
+    * decode_ragged_by_length: B=3 H=4 with lengths 5000/1300/129 split over
+      the ranks by held tokens.
+    * outproj_<transport>: y = sum over ranks of o_r [256, 256] @ w_r [256, 256].
+    """
+    import numpy as np
+    import torch
+    from oracle import attention as orc
+    from pallas_flash.distributed import collectives
+    from pallas_flash.distributed.outproj import out_proj_all_reduce
+    from pallas_flash.kernels import decoding as dec
+    from pallas_flash.ops import interface as pf
+
+    f = lambda t: t.detach().float().cpu().numpy()
+    out = {}
+
+    def rec(name, actual, expected, rel_tol, abs_tol=None):
+        r = orc.compare(actual, expected)
+        out[name] = [r["max_abs"], r["rel"], rel_tol, abs_tol]
+
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        group = dist.group.WORLD
+    # head-partitioned causal forward + backward
+    rng = np.random.Generator(np.random.PCG64(101))
+    Hg, Np, Dp = 2 * world, 384, 128
+    full = [rng.standard_normal((1, Hg, Np, Dp), dtype=np.float32) for _ in range(4)]
+    loc = [torch.from_numpy(x[:, 2 * rank:2 * rank + 2].copy()).to(torch.bfloat16) for x in full]
+    q, k, v, do = (t.cuda() for t in loc)
+    o, lse = pf.flash_attention_forward(q, k, v, causal=True)
+    dq, dk, dv = pf.flash_attention_backward(q, k, v, o, lse, do, causal=True)
+    qn, kn, vn, don = (f(t) for t in loc)
+    ro, rl = orc.mha_forward(qn, kn, vn, causal=True)
+    rdq, rdk, rdv = orc.mha_backward(qn, kn, vn, ro, rl, don, causal=True)
+    rec("attn_fwd_o", f(o), ro, PARITY_TOL["o_rel"], PARITY_TOL["o_max_abs"])
+    rec("attn_fwd_lse", f(lse), rl, float("inf"), PARITY_TOL["lse_abs"])
+    for name, got, ref in (("attn_bwd_dq", dq, rdq), ("attn_bwd_dk", dk, rdk), ("attn_bwd_dv", dv, rdv)):
+        rec(name, f(got), ref, PARITY_TOL["grad_rel"])
+    # sequence-sharded decode over each transport
+    rng = np.random.Generator(np.random.PCG64(102))
+    Bd, Hd, nl, Dd = 1, 8, 1024, 128
+    qd = torch.from_numpy(rng.standard_normal((Bd, Hd, 1, Dd), dtype=np.float32)).half()
+    kd = torch.from_numpy(rng.standard_normal((Bd, Hd, nl * world, Dd), dtype=np.float32)).half()
+    vd = torch.from_numpy(rng.standard_normal((Bd, Hd, nl * world, Dd), dtype=np.float32)).half()
+    ro, rl = orc.decode_forward(f(qd), f(kd), f(vd))
+    kl = kd[:, :, rank * nl:(rank + 1) * nl].contiguous().cuda()
+    vl = vd[:, :, rank * nl:(rank + 1) * nl].contiguous().cuda()
+    transports = ("peer", "nccl", "lib") if world > 1 else ("single",)
+    for t in transports:
+        kw = {"group": group, "transport": t} if world > 1 else {}
+        o, lse = dec.pallas_flash_decoding(qd.cuda(), kl, vl, return_lse=True, **kw)
+        rec(f"decode_{t}_o", f(o), ro, PARITY_TOL["o_rel"], PARITY_TOL["o_max_abs"])
+        rec(f"decode_{t}_lse", f(lse), rl, float("inf"), PARITY_TOL["lse_abs"])
+    # ragged batch sharded by held tokens
+    rng = np.random.Generator(np.random.PCG64(103))
+    lens = np.array([5000, 1300, 129])
+    Br, Hr, Nr = 3, 4, 5120
+    qr = torch.from_numpy(rng.standard_normal((Br, Hr, 1, Dd), dtype=np.float32)).half()
+    kr = torch.from_numpy(rng.standard_normal((Br, Hr, Nr, Dd), dtype=np.float32)).half()
+    vr = torch.from_numpy(rng.standard_normal((Br, Hr, Nr, Dd), dtype=np.float32)).half()
+    ro, rl = orc.decode_forward(f(qr), f(kr), f(vr), kv_lens=lens)
+    if world > 1:
+        kl, vl, ll = collectives.shard_by_length(kr, vr, lens, rank, world)
+        o = dec.pallas_flash_decoding(qr.cuda(), kl.cuda(), vl.cuda(), kv_lens=ll.cuda(), group=group,
+                                      transport="peer", sharding="by_length")
+    else:
+        o = dec.pallas_flash_decoding(qr.cuda(), kr.cuda(), vr.cuda(),
+                                      kv_lens=torch.from_numpy(lens).cuda())
+    rec("decode_ragged_by_length_o", f(o), ro, PARITY_TOL["o_rel"], PARITY_TOL["o_max_abs"])
+    # fused out-projection + all-reduce
+    To, Ko, No = 256, 256, 256
+    ows = []
+    for r in range(world):
+        g = np.random.Generator(np.random.PCG64(200 + r))
+        ows.append((torch.from_numpy(g.standard_normal((To, Ko), dtype=np.float32)).to(torch.bfloat16),
+                    torch.from_numpy(g.standard_normal((Ko, No), dtype=np.float32) / Ko ** 0.5)
+                    .to(torch.bfloat16)))
+    yref = sum(f(a).astype(np.float64) @ f(b).astype(np.float64) for a, b in ows)
+    grp = group if world > 1 else single_rank_group()
+    for t in (("peer", "nccl") if world > 1 else ("peer",)):
+        y = out_proj_all_reduce(ows[rank][0].cuda(), ows[rank][1].cuda(), grp, transport=t)
+        rec(f"outproj_{t}", f(y), yref, PARITY_TOL["o_rel"], 2e-2 * float(np.abs(yref).max()))
+    torch.cuda.synchronize()
+    from pallas_flash import _lib
+    code, detail = _lib.device_status()
+    if code != 0:
+        raise RuntimeError(f"device status {code} at site {detail} during the parity checks")
+    # worst over the ranks
+    names = sorted(out)
+    vals = torch.tensor([[out[n][0], out[n][1]] for n in names], dtype=torch.float64, device="cuda")
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    res = {}
+    for i, n in enumerate(names):
+        mx, rel = float(vals[i, 0]), float(vals[i, 1])
+        rel_tol, abs_tol = out[n][2], out[n][3]
+        ok = rel <= rel_tol and (abs_tol is None or mx <= abs_tol)
+        res[n] = {"max_abs": float(f"{mx:.3g}"), "rel": float(f"{rel:.3g}"), "ok": bool(ok)}
+    return res
+
+
+# ---------------------------------------------------------------------------
 # GPU measurements
 # ---------------------------------------------------------------------------
 def bench_attention(steps: int, warmup: int, rank: int, world: int, clocks: ClockSampler):
@@ -274,6 +411,47 @@ def bench_attention(steps: int, warmup: int, rank: int, world: int, clocks: Cloc
     if code != 0:
         raise RuntimeError(f"device status {code} at site {detail}")
     return total_ms, fwd_ms, bwd_ms
+
+
+C1_B, C1_H, C1_N = 1, 4, 1024
+C1_FLOPS = 4 * C1_B * C1_H * C1_N * C1_N * D * 0.5        # causal
+
+
+def bench_c1(steps: int, warmup: int) -> float:
+    """Causal forward B=1 H=4 N=1024 D=128 (the reference's CPU baseline_mha
+    configuration) on one GPU: median microseconds per call, L2 flushed
+    before every call (the inputs, 3 MB, would otherwise stay in L2)."""
+    import torch
+    from pallas_flash.ops import interface as pf
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7000)
+    shape = (C1_B, C1_H, C1_N, D)
+    q, k, v = (torch.randn(shape, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+    o = torch.empty_like(q)
+    lse = torch.empty((C1_B, C1_H, C1_N), device="cuda", dtype=torch.float32)
+
+    def step():
+        pf.flash_attention_forward(q, k, v, causal=True, out=o, lse=lse)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    return _timed(step, steps, L2Flush(), torch.cuda.current_stream())
+
+
+def cpu_c1_sample():
+    """The oracle's causal baseline_mha restatement (numpy fp32) on the c1
+    shape: best of 3 runs, seconds."""
+    import numpy as np
+    from oracle import attention as orc
+    rng = np.random.Generator(np.random.PCG64(7))
+    q, k, v = (rng.standard_normal((C1_B, C1_H, C1_N, D), dtype=np.float32) for _ in range(3))
+    best = float("inf")
+    for _ in range(3):
+        t0 = time.perf_counter()
+        orc.mha_forward(q, k, v, causal=True, dtype=np.float32, row_chunk=C1_N)
+        best = min(best, time.perf_counter() - t0)
+    return best
 
 
 LONG_B, LONG_H, LONG_N = 1, 32, 16384
@@ -457,39 +635,49 @@ def _timed(fn, steps, flush, stream, world: int = 1):
 
 
 def bench_ragged_decode(steps: int, warmup: int, rank: int, world: int):
-    """Batched ragged decode (B=8, H=16, D=128, fp16, lengths U[4096, 131072]):
-    the dense padded cache sequence-sharded over the ranks, and (one GPU) the
-    same tokens in a paged cache of 64-token pages in shuffled order.
-    Returns (dense us, paged us or None, algorithmic bytes of all ranks)."""
+    """Batched ragged decode (B=8, H=16, D=128, fp16, lengths U[4096, 131072]).
+    One GPU: the dense padded cache, and the same tokens in a paged cache of
+    64-token pages in shuffled order.  Several GPUs: every rank holds an equal
+    slice of every sequence's held tokens (length-balanced sharding), and,
+    for comparison, contiguous chunks of the padded capacity.
+    Returns (dense us, paged us or None, contiguous us or None, algorithmic
+    bytes of all ranks)."""
     import numpy as np
     import torch
+    from pallas_flash.distributed import collectives
     from pallas_flash.kernels import decoding as dec
     from pallas_flash.kernels import paged
 
     lens = ragged_lens()
-    n_local = RAG_NCAP // world
     g = torch.Generator(device="cuda")
     g.manual_seed(4000 + rank)
     q = torch.randn((RAG_B, RAG_H, 1, RAG_D), device="cuda", generator=g).to(torch.float16)
-    k = torch.randn((RAG_B, RAG_H, n_local, RAG_D), device="cuda", generator=g).to(torch.float16)
-    v = torch.randn((RAG_B, RAG_H, n_local, RAG_D), device="cuda", generator=g).to(torch.float16)
-    lens_t = torch.from_numpy(lens).cuda()
     flush = L2Flush()
     stream = torch.cuda.current_stream()
     group = None
     if world > 1:
         import torch.distributed as dist
         group = dist.group.WORLD
-
-    def dense():
-        return dec.pallas_flash_decoding(q, k, v, kv_lens=lens_t, group=group, transport="peer")
-
+    nbytes = int(lens.astype(np.int64).sum()) * RAG_H * RAG_D * 2 * 2
+    paged_us = contiguous_us = None
+    if world == 1:
+        k = torch.randn((RAG_B, RAG_H, RAG_NCAP, RAG_D), device="cuda", generator=g).to(torch.float16)
+        v = torch.randn((RAG_B, RAG_H, RAG_NCAP, RAG_D), device="cuda", generator=g).to(torch.float16)
+        lens_t = torch.from_numpy(lens).cuda()
+        dense = lambda: dec.pallas_flash_decoding(q, k, v, kv_lens=lens_t)
+    else:
+        starts, counts = collectives.length_balanced_split(lens, world)
+        cap = int(-(-int(counts.max()) // 128) * 128)
+        k = torch.randn((RAG_B, RAG_H, cap, RAG_D), device="cuda", generator=g).to(torch.float16)
+        v = torch.randn((RAG_B, RAG_H, cap, RAG_D), device="cuda", generator=g).to(torch.float16)
+        lens_t = torch.from_numpy(counts[rank].astype(np.int32)).cuda()
+        dense = lambda: dec.pallas_flash_decoding(q, k, v, kv_lens=lens_t, group=group, transport="peer",
+                                                  sharding="by_length")
     for _ in range(warmup):
         dense()
     torch.cuda.synchronize()
     barrier(world)
     dense_us = allreduce_max(_timed(dense, steps, flush, stream, world), world)
-    paged_us = None
     if world == 1:
         cache = paged.PagedKVCache.from_dense(k, v, lens, page_size=RAG_PAGE, shuffle_seed=1)
         del k, v
@@ -501,8 +689,20 @@ def bench_ragged_decode(steps: int, warmup: int, rank: int, world: int):
             run_paged()
         torch.cuda.synchronize()
         paged_us = _timed(run_paged, steps, flush, stream)
-    nbytes = int(lens.astype(np.int64).sum()) * RAG_H * RAG_D * 2 * 2
-    return dense_us, paged_us, nbytes
+    else:
+        del k, v
+        n_local = RAG_NCAP // world
+        kc = torch.randn((RAG_B, RAG_H, n_local, RAG_D), device="cuda", generator=g).to(torch.float16)
+        vc = torch.randn((RAG_B, RAG_H, n_local, RAG_D), device="cuda", generator=g).to(torch.float16)
+        glens = torch.from_numpy(lens).cuda()
+        contig = lambda: dec.pallas_flash_decoding(q, kc, vc, kv_lens=glens, group=group, transport="peer")
+        for _ in range(warmup):
+            contig()
+        torch.cuda.synchronize()
+        barrier(world)
+        contiguous_us = allreduce_max(_timed(contig, steps, flush, stream, world), world)
+        del kc, vc
+    return dense_us, paged_us, contiguous_us, nbytes
 
 
 OP_T, OP_K, OP_N = 4 * 4096, 16 * 128, 2048
@@ -526,11 +726,7 @@ def bench_outproj(steps: int, warmup: int, rank: int, world: int):
         import torch.distributed as dist
         group = dist.group.WORLD
     else:
-        import torch.distributed as dist
-        if not dist.is_initialized():
-            dist.init_process_group("gloo", init_method="tcp://127.0.0.1:" + str(_free_port()),
-                                    rank=0, world_size=1)
-        group = dist.group.WORLD
+        group = single_rank_group()
     stream = torch.cuda.current_stream()
     out = {}
     for transport in ("peer", "nccl"):
@@ -664,6 +860,7 @@ def main():
         op = bench_outproj(args.steps, warmup, rank, world)
         print(f"out-projection leg: {op['peer']:.1f} us/step", flush=True)
         return
+    parity = run_parity(rank, world) if args.profile_leg is None else None
     clocks = ClockSampler(local).start()
     total_ms, fwd_ms, bwd_ms = bench_attention(args.steps, warmup, rank, world, clocks)
     clk = clocks.stop()
@@ -678,23 +875,23 @@ def main():
     dec_steps = max(5, min(args.steps, 50))
     dec_us, dec_kus, dec_bytes = bench_decode(dec_steps, warmup, rank, world, "peer")
     nccl_us = bench_decode(dec_steps, warmup, rank, world, "nccl")[0] if world > 1 else None
-    rag_us, rag_paged_us, rag_bytes = bench_ragged_decode(max(5, min(args.steps, 20)), warmup,
-                                                          rank, world)
+    rag_us, rag_paged_us, rag_contig_us, rag_bytes = bench_ragged_decode(max(5, min(args.steps, 20)),
+                                                                         warmup, rank, world)
     gqa = bench_gqa_decode(max(5, min(args.steps, 50)), warmup) if world == 1 else None
+    c1_us = bench_c1(max(10, min(args.steps, 50)), warmup) if world == 1 else None
     long_ms = bench_attention_long(max(3, min(args.steps, 5)), warmup) if world == 1 else None
     op = bench_outproj(max(5, min(args.steps, 20)), warmup, rank, world)
 
     if rank == 0:
         bwd_flops = FWD_FLOPS * 2.5
         achieved = bwd_flops / (bwd_ms_max * 1e-3) / 1e12
-        roof = {"kernel": "attn_bwd (prep + dK/dV + dQ kernels, one pu_attn_bwd call)",
+        roof = {"kernel": "attn_bwd (prep + fused dK/dV/dQ + dQ conversion kernels, one pu_attn_bwd call)",
                 "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                 "peak_source": peaks["source"] + " bf16 burst",
                 "traffic": NCU_TRAFFIC_BYTES["attn_bwd"],
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, "
-                                  "profiles/attn_bwd_*_causal_B4H16N4096D128.md; above the "
-                                  "algorithmic bytes because heavy-first order re-reads from DRAM"}
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch: "
+                                  + TRAFFIC_CAPTURE}
         fwd_ach = FWD_FLOPS / (fwd_ms_max * 1e-3) / 1e12
         cpu = None
         if world == 1:
@@ -748,11 +945,12 @@ def main():
         line["decode_ragged"] = {
             "workload": f"ragged split-KV decode B={RAG_B} H={RAG_H} D={RAG_D} fp16, lengths "
                         f"U[4096,{RAG_NCAP}] rounded to 128 (seeded), dense cache padded to "
-                        f"{RAG_NCAP} and sequence-sharded over {world} GPU(s)",
+                        f"{RAG_NCAP}, sequence-sharded over {world} GPU(s)",
             "algorithmic_bytes": rag_bytes,
             "dense": {"us_per_step": round(rag_us, 2),
                       "GB_s": round(rag_bytes / (rag_us * 1e-6) / 1e9, 1),
-                      "frac": round(rag_bytes / (rag_us * 1e-6) / 1e9 / (hbm * world), 4)},
+                      "frac": round(rag_bytes / (rag_us * 1e-6) / 1e9 / (hbm * world), 4),
+                      "sharding": "by held tokens (length_balanced_split)" if world > 1 else "one GPU"},
             "l2": "1 GiB buffer written, then another 1 GiB read, before every step"}
         op_flops = 2 * OP_T * OP_K * OP_N
         link_bytes = 2 * (world - 1) * OP_T * OP_N * 2 // world   # partials out + results out, per rank
@@ -790,6 +988,25 @@ def main():
                     "us_per_step": round(us, 2), "kv_bytes": nbytes,
                     "GB_s": round(nbytes / (us * 1e-6) / 1e9, 1),
                     "frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4)}
+        if rag_contig_us is not None:
+            line["decode_ragged"]["dense_contiguous_chunks"] = {
+                "us_per_step": round(rag_contig_us, 2),
+                "GB_s": round(rag_bytes / (rag_contig_us * 1e-6) / 1e9, 1),
+                "frac": round(rag_bytes / (rag_contig_us * 1e-6) / 1e9 / (hbm * world), 4),
+                "sharding": "rank r holds positions [r*N/G, (r+1)*N/G) of the padded capacity"}
+        if c1_us is not None:
+            c1_cpu_s = cpu_c1_sample()
+            line["attn_c1"] = {
+                "workload": f"causal forward B={C1_B} H={C1_H} N={C1_N} D={D} bf16 (the reference's "
+                            "CPU baseline_mha configuration), one GPU, L2 flushed before each call",
+                "us_per_call": round(c1_us, 2),
+                "TFLOP_s": round(C1_FLOPS / (c1_us * 1e-6) / 1e12, 1),
+                "frac": round(C1_FLOPS / (c1_us * 1e-6) / 1e12 / peaks["bf16_tflops"], 4),
+                "cpu_baseline": {"value": round(c1_cpu_s * 1e6, 1), "unit": "us/call",
+                                 "cores": cpu_threads(), "kind": "port",
+                                 "sample": "whole workload, oracle causal baseline_mha restatement, "
+                                           "numpy fp32, best of 3"}}
+        line["parity"] = parity
         if rag_paged_us is not None:
             line["decode_ragged"]["paged"] = {
                 "page_size": RAG_PAGE, "page_order": "shuffled",
@@ -813,32 +1030,43 @@ def main():
             from pallas_flash.distributed import peer
             peer.close_all()
             dist.destroy_process_group()
+    if parity is not None and not all(v["ok"] for v in parity.values()):
+        bad = [k for k, v in parity.items() if not v["ok"]]
+        print(f"parity miss: {bad}", file=sys.stderr, flush=True)
+        sys.exit(1)
 
 
 def run_reference(args, warmup):
     """The reference algorithm on host CPU cores (numpy port of its pure-JAX
-    path; JAX is not installed).  Rank 0 only."""
+    path; JAX is not installed).  Rank 0 only.  Each step is a bounded sample:
+    the fwd+bwd of one of the 64 (b, h) heads of a GPU's workload; the line
+    reports that sample's measured time and the throughput it implies."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    vals = []
+    vals, times = [], []
     sample = ""
     for i in range(warmup + args.steps):
         v, dt, sample = cpu_attention_sample(heads=1)
         if i >= warmup:
             vals.append(v)
+            times.append(dt)
     value = statistics.median(vals)
-    # the CPU restatement is one host: its throughput does not grow with GPUs
-    step_ms = STEP_FLOPS * world / (value * 1e12) * 1e3
+    sample_ms = statistics.median(times) * 1e3
+    heads = B * H
     line = {
         "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "TFLOP/s",
-        "n_gpus": world, "steps": args.steps, "warmup": warmup, "ms_per_step": round(step_ms, 1),
+        "n_gpus": world, "steps": args.steps, "warmup": warmup, "ms_per_step": round(sample_ms, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic N(0,1) inputs (seeded numpy PCG64)",
         "config": {"workload": "causal flash-attention fwd+bwd, B=4 H=16 N=4096 D=128 per GPU",
                    "global_batch": B, "seq_len": N, "heads_per_gpu": H, "head_dim": D,
                    "parallelism": f"heads{world}"},
+        "sample": {"heads_per_step": 1, "of_heads": heads, "measured_ms_per_step": round(sample_ms, 1),
+                   "extrapolated_full_step_ms": round(sample_ms * heads, 1),
+                   "note": "ms_per_step is the measured one-head sample; value is its FLOPs / time "
+                           "(the whole workload would take extrapolated_full_step_ms on this host)"},
         "cpu_baseline": {"value": round(value, 4), "kind": "port", "cores": cpu_threads(),
                          "sample": sample + " per step; JAX reference not installable here, so the "
                                             "numpy restatement in oracle/ stands in"},
