@@ -168,3 +168,29 @@ def test_gqa_growing_scores(mods):
     ro, rl = orc.decode_forward(_f(q), _f(k), _f(v))
     assert_close_o(_f(o), ro, what="growing scores")
     assert_close_lse(_f(lse), rl)
+
+
+@pytest.mark.parametrize("H,H_kv", [(32, 8), (16, 16)])
+def test_fp8_cache_every_code(mods, H, H_kv):
+    """Every finite e4m3 code, subnormals and the largest magnitudes included,
+    appears in K and V; the kernel decodes them exactly (the oracle sees the
+    same dequantised values).  Scores stay small so all rows matter."""
+    _lib, dec = mods
+    fp8 = getattr(torch, "float8_e4m3fn", None)
+    if fp8 is None:
+        pytest.skip("torch without float8_e4m3fn")
+    B, N, D = 1, 2032, 128
+    codes = torch.tensor([c for c in range(256) if c not in (0x7F, 0xFF)], dtype=torch.uint8)
+    idx = (torch.arange(N)[:, None] * 7 + torch.arange(D)[None, :] * 3) % codes.numel()
+    k8 = codes[idx].view(fp8).expand(B, H_kv, N, D).contiguous().cuda()
+    v8 = codes[(idx + 101) % codes.numel()].view(fp8).expand(B, H_kv, N, D).contiguous().cuda()
+    q = _gen((B, H, 1, D), 23, torch.float16, 0.02)
+    k_scale, v_scale = 1.0 / 448.0, 1.0 / 32.0
+    o, lse = dec.pallas_flash_decoding(q, k8, v8, return_lse=True, k_scale=k_scale, v_scale=v_scale)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == (0, 0)
+    kd = _f(k8) * k_scale
+    vd = _f(v8) * v_scale
+    ro, rl = orc.decode_forward(_f(q), kd, vd, scale=1 / math.sqrt(D))
+    assert_close_o(_f(o), ro, what="fp8 every code")
+    assert_close_lse(_f(lse), rl)
