@@ -362,19 +362,19 @@ def run_parity(rank: int, world: int) -> dict:
 # ---------------------------------------------------------------------------
 # GPU measurements
 # ---------------------------------------------------------------------------
-def bench_attention(steps: int, warmup: int, rank: int, world: int, clocks: ClockSampler):
+def bench_attention(steps: int, warmup: int, rank: int, world: int, clocks: ClockSampler, batch: int = B):
     import torch
     from pallas_flash.ops import interface as pf
 
     g = torch.Generator(device="cuda")
     g.manual_seed(1000 + rank)
-    shape = (B, H, N, D)
+    shape = (batch, H, N, D)
     q, k, v, do = (torch.randn(shape, device="cuda", dtype=torch.float32, generator=g).to(torch.bfloat16)
                    for _ in range(4))
     o = torch.empty_like(q)
-    lse = torch.empty((B, H, N), device="cuda", dtype=torch.float32)
+    lse = torch.empty((batch, H, N), device="cuda", dtype=torch.float32)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    ws = torch.empty(pf.bwd_workspace_bytes(B, H, N, D), device="cuda", dtype=torch.uint8)
+    ws = torch.empty(pf.bwd_workspace_bytes(batch, H, N, D), device="cuda", dtype=torch.uint8)
     stream = torch.cuda.current_stream()
 
     def step(ev=None):
@@ -839,6 +839,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--profile-leg", choices=["attn", "decode", "gqa", "outproj"], default=None,
                     help="run only this leg and print no JSON (small runs for ncu captures)")
+    ap.add_argument("--profile-batch", type=int, default=B,
+                    help="batch of the attention profile leg (default: the bench workload's)")
     args = ap.parse_args()
     warmup = max(3, args.warmup)
     peaks = load_peaks()
@@ -862,7 +864,8 @@ def main():
         return
     parity = run_parity(rank, world) if args.profile_leg is None else None
     clocks = ClockSampler(local).start()
-    total_ms, fwd_ms, bwd_ms = bench_attention(args.steps, warmup, rank, world, clocks)
+    total_ms, fwd_ms, bwd_ms = bench_attention(args.steps, warmup, rank, world, clocks,
+                                               batch=args.profile_batch if args.profile_leg else B)
     clk = clocks.stop()
     if args.profile_leg == "attn":
         print(f"attention leg: {total_ms / args.steps:.3f} ms/step", flush=True)
