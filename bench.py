@@ -761,8 +761,8 @@ def _free_port() -> int:
 
 def bench_gqa_decode(steps: int, warmup: int):
     """Grouped-head decode on one GPU: B=1, 32 query heads over 8 K/V heads,
-    32768 tokens, D=128, fp16 (tensor-core kernel) and fp8 (e4m3, CUDA-core
-    kernel) caches; then the ragged batch of the decode_ragged leg (B=8,
+    32768 tokens, D=128, fp16 and fp8 (e4m3) caches (both on the tensor-core
+    kernel); then the ragged batch of the decode_ragged leg (B=8,
     lengths U[4096, 131072]) with 32 query heads over 8 K/V heads, fp16.
     Returns {case: (us, K/V bytes read)}."""
     import torch
@@ -983,8 +983,9 @@ def main():
         if gqa:
             line["decode_gqa"] = {
                 "workload": "grouped-head decode B=1 H=32 H_kv=8 N=32768 D=128, one GPU (f16: "
-                            "gqa_tc_kernel, tcgen05 K-tile x query-group; fp8_e4m3: gqa_kernel, CUDA "
-                            "cores); ragged_f16: B=8 H=32 H_kv=8 D=128 with the decode_ragged lengths",
+                            "gqa_tc_kernel, tcgen05 kind::f16 K-tile x query-group; fp8_e4m3: the "
+                            "same kernel with kind::f8f6f4 products on the e4m3 tiles); ragged_f16: "
+                            "B=8 H=32 H_kv=8 D=128 with the decode_ragged lengths",
                 "l2": "1 GiB buffer written, then another 1 GiB read, before every step"}
             for name, (us, nbytes) in gqa.items():
                 line["decode_gqa"][name] = {

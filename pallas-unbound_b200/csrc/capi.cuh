@@ -87,6 +87,12 @@ int make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_
                       box_rows, swizzle128);
 }
 
+int make_tmap_u8_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t outer,
+                    uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+  return make_tmap_3d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, cols, rows, outer, box_cols, box_rows,
+                      swizzle128);
+}
+
 int make_tmap_f32_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
                      uint64_t outer, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
   return make_tmap_3d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, cols, rows, outer, box_cols,

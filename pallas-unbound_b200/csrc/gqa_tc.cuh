@@ -34,7 +34,8 @@
 //   all            the last CTA of a (b, K/V head, slice) merges the split
 //                  records of its heads at once (weights in the idle ring)
 //
-// TMEM (64 columns): S_0 [0,16), S_1 [16,32), Oᵀ [32,48).
+// TMEM (64 columns): S_0 [0,16), S_1 [16,32), Oᵀ [32,48); e4m3 caches: Oᵀ of
+// each P part at [32 + 16 k, 48 + 16 k) (128 columns allocated).
 // Rows past the chunk's end inside the last tile are masked to -inf; their V
 // rows are zeroed in shared memory before the P·V product (so stale cache
 // contents cannot reach the output).  Every wait is bounded; the softmax
@@ -58,21 +59,45 @@ constexpr int kTileBytes = BT * kDim * 2;  // one K or V tile
 constexpr float kRescaleLog2 = 8.f;
 static_assert(kThreads == 256, "the softmax warps are 0-3, producer 4, issuer 5");
 
-template <int NP>
+// Cache tiles of one element type: 16-bit tiles are two 64-column swizzle
+// blocks (32 KB), e4m3 tiles one 128-column block (16 KB).  A 16-bit CTA
+// takes an SM (192 KB ring).  e4m3 CTAs either take an SM with a 6-stage
+// ring or, with kF8CtasPerSm = 2, share one with 2-stage rings (two CTAs of
+// 3 stages would need 2 x 115 KB) so their per-tile chains (products,
+// softmax, products) interleave.
+constexpr int kF8CtasPerSm = 1;
+
+template <typename KVT>
+struct Ring {
+  static constexpr int kTileBytes = BT * kDim * (int)sizeof(KVT);
+  static constexpr int NS = sizeof(KVT) == 1 ? (kF8CtasPerSm == 1 ? 6 : 2) : 3;
+};
+
+// Shared memory.  16-bit: the query group [NP x 128] and each Pᵀ buffer
+// [NP x 128 rows] are two 64-column blocks.  fp8: kParts e4m3 parts (one
+// 128-column block each) of the scaled queries and of each Pᵀ, whose sum
+// carries about 12 significant bits, the precision of f16.
+constexpr int kParts = 3;
+
+template <int NP, typename KVT = __half>
 struct Cfg {
-  static constexpr int kBlock = NP * 128;                  // bytes of one 64-column swizzle block
-  static constexpr int kQBytes = 2 * kBlock;               // query group [NP x 128], K-major
-  static constexpr int kPBytes = 2 * kBlock;               // Pᵀ [NP x 128 rows], K-major
+  static constexpr int NS = Ring<KVT>::NS;
+  static constexpr int kBlock = NP * 128;                  // bytes of one swizzle block of NP rows
+  static constexpr int kQBytes = (sizeof(KVT) == 1 ? kParts : 2) * kBlock;
+  static constexpr int kPBytes = (sizeof(KVT) == 1 ? kParts : 2) * kBlock;
   static constexpr int kOffQ = 0;
   static constexpr int kOffP = kOffQ + kQBytes;            // two buffers
   static constexpr int kOffKV = kOffP + 2 * kPBytes;       // stage s: K, then V
-  static constexpr int kOffBar = kOffKV + NS * 2 * kTileBytes;
+  static constexpr int kOffBar = kOffKV + NS * 2 * Ring<KVT>::kTileBytes;
   // full[NS], empty[NS], s_full[2], p_full[2], p_free[2], drain
   static constexpr int kNumBars = 2 * NS + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem base, abort flag, last-CTA flag
   static constexpr int kOffRed = kOffMisc + 16;            // [4][NP] floats
-  static constexpr int kSmemBytes = kOffRed + 4 * NP * 4;
-  static constexpr uint32_t kTmemCols = NP <= 16 ? 64 : 128;
+  static constexpr int kOffQinv = kOffRed + 4 * NP * 4;    // fp8: [NP] per-head factor undoing the query scale
+  static constexpr int kSmemBytes = kOffQinv + NP * 4;
+  // S_0, S_1, then one O^T accumulator (16-bit) or kParts of them (e4m3: one
+  // per P part, combined with weights kPartScale^-part at the end)
+  static constexpr uint32_t kTmemCols = (NP <= 16 && sizeof(KVT) == 2) ? 64 : 128;
   static_assert(kOffP % 1024 == 0 && kPBytes % 1024 == 0 && kOffKV % 1024 == 0,
                 "swizzled operands start on 1024-byte boundaries");
 };
@@ -89,6 +114,31 @@ __device__ __forceinline__ void tmem_st_np(uint32_t taddr, const uint32_t (&r)[N
   else tmem_st32(taddr, r);
 }
 
+// (a, b) as kParts e4m3 pairs: part i is the e4m3 rounding (saturating) of
+// what the previous parts left, multiplied by kPartScale^i when `scaled` (so
+// a remainder stays in e4m3's normal range instead of its 2^-9-step
+// subnormals), so (a, b) ~ sum_i part_i / kPartScale^i (scaled) or
+// sum_i part_i.
+constexpr float kPartScale = 16.f;
+
+template <bool scaled>
+__device__ __forceinline__ void split_e4m3(float a, float b, uint16_t (&part)[kParts]) {
+#pragma unroll
+  for (int i = 0; i < kParts; ++i) {
+    const __nv_fp8x2_storage_t h2 = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+    part[i] = (uint16_t)h2;
+    if (i + 1 < kParts) {
+      const float2 hf = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(h2, __NV_E4M3)));
+      a -= hf.x;
+      b -= hf.y;
+      if (scaled) {
+        a *= kPartScale;
+        b *= kPartScale;
+      }
+    }
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ uint16_t to16(float x);
 template <>
@@ -103,11 +153,15 @@ __device__ __forceinline__ uint16_t to16<__nv_bfloat16>(float x) {
 // neighbours in the grid and read the same K/V tiles at the same time, so
 // all but the first read come from L2.  The per-head loops run over NP with
 // the heads past the slice skipped.
-template <typename T, int NP>
+template <typename T, typename KVT, int NP>
 __global__ void __launch_bounds__(kThreads, 1)
     gqa_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const Params p) {
-  using C = Cfg<NP>;
+  using C = Cfg<NP, KVT>;
+  constexpr int NS = C::NS;
+  constexpr int kTileBytes = Ring<KVT>::kTileBytes;
+  constexpr bool kF8 = sizeof(KVT) == 1;
+  static_assert(!kF8 || NP == 16, "fp8 caches use 16-head slices");
   static_assert(NP == 16 || NP == 32, "padded group size");
   const int Gt = p.group;                       // query heads per K/V head
   const int n_slices = (Gt + NP - 1) / NP;
@@ -150,11 +204,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // query group -> sQ (K-major, 128-byte swizzle; rows G..NP-1 zero); both
   // Pᵀ buffers zeroed (rows G..NP-1 are never written afterwards)
-  for (int c = tid; c < NP * 16; c += kThreads) {
-    const int n = c >> 4, cr = c & 15, cb = cr >> 3, ch = cr & 7;
-    uint4 w = make_uint4(0u, 0u, 0u, 0u);
-    if (n < G) w = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (size_t)(bh0 + n) * kDim + cr * 8);
-    *reinterpret_cast<uint4*>(sQ + cb * C::kBlock + n * 128 + ((ch ^ (n & 7)) << 4)) = w;
+  float* s_qinv = reinterpret_cast<float*>(smem + C::kOffQinv);
+  if constexpr (kF8) {
+    // head n = tid / 16, elements 8*cr .. 8*cr+7: scaled by a power of two so
+    // the head's largest |q| lands in [128, 256), then split into kParts
+    // e4m3 parts
+    const int n = tid >> 4, cr = tid & 15;
+    float x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = 0.f;
+    if (n < G) {
+      const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (size_t)(bh0 + n) * kDim + cr * 8);
+      unpack8<T>(w, x);
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(x[i]));
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const int e = (mx > 0.f && isfinite(mx)) ? ((__float_as_int(mx) >> 23) & 0xff) - 127 : 7;
+    const int sh = max(-100, min(100, 7 - e));
+    const float up = __int_as_float((127 + sh) << 23), down = __int_as_float((127 - sh) << 23);
+    uint32_t w[kParts][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint16_t pr[kParts];
+      split_e4m3<false>(x[2 * i] * up, x[2 * i + 1] * up, pr);
+#pragma unroll
+      for (int k = 0; k < kParts; ++k)
+        w[k][i >> 1] = (i & 1) ? (w[k][i >> 1] | ((uint32_t)pr[k] << 16)) : (uint32_t)pr[k];
+    }
+    const int off = n * 128 + ((((cr >> 1) ^ (n & 7))) << 4) + (cr & 1) * 8;
+#pragma unroll
+    for (int k = 0; k < kParts; ++k) *reinterpret_cast<uint2*>(sQ + k * C::kBlock + off) = make_uint2(w[k][0], w[k][1]);
+    if (cr == 0) s_qinv[n] = n < G ? down : 0.f;
+  } else {
+    for (int c = tid; c < NP * 16; c += kThreads) {
+      const int n = c >> 4, cr = c & 15, cb = cr >> 3, ch = cr & 7;
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (n < G) w = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (size_t)(bh0 + n) * kDim + cr * 8);
+      *reinterpret_cast<uint4*>(sQ + cb * C::kBlock + n * 128 + ((ch ^ (n & 7)) << 4)) = w;
+    }
   }
   for (int c = tid; c < 2 * C::kPBytes / 16; c += kThreads)
     reinterpret_cast<uint4*>(sP)[c] = make_uint4(0u, 0u, 0u, 0u);
@@ -197,8 +287,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* dV = dK + kTileBytes;
         const int row = t_begin + i * BT;
         mbar_arrive_expect_tx(bFull + s, 2 * kTileBytes);
-        for (int cb = 0; cb < 2; ++cb) tma_load_3d(dK + cb * BT * 128, &tmK, bFull + s, cb * 64, row, bkv);
-        for (int cb = 0; cb < 2; ++cb) tma_load_3d(dV + cb * BT * 128, &tmV, bFull + s, cb * 64, row, bkv);
+        if constexpr (kF8) {
+          tma_load_3d(dK, &tmK, bFull + s, 0, row, bkv);
+          tma_load_3d(dV, &tmV, bFull + s, 0, row, bkv);
+        } else {
+          for (int cb = 0; cb < 2; ++cb) tma_load_3d(dK + cb * BT * 128, &tmK, bFull + s, cb * 64, row, bkv);
+          for (int cb = 0; cb < 2; ++cb) tma_load_3d(dV + cb * BT * 128, &tmV, bFull + s, cb * 64, row, bkv);
+        }
         ++issued;
       }
       // copies still in flight land before the CTA may exit
@@ -210,19 +305,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- tcgen05 issuer ----------------
     if (lane == 0) {
       constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-      constexpr uint32_t idS = make_idesc_16(BT, NP, 0, 0, kBf16);
-      constexpr uint32_t idO = make_idesc_16(kDim, NP, 1, 0, kBf16);
+      constexpr uint32_t idS = kF8 ? make_idesc_e4m3(BT, NP, 0, 0) : make_idesc_16(BT, NP, 0, 0, kBf16);
+      constexpr uint32_t idO = kF8 ? make_idesc_e4m3(kDim, NP, 1, 0) : make_idesc_16(kDim, NP, 1, 0, kBf16);
       const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t dP0 = make_sdesc_sw128(smem_u32(sP), 16, 1024);
       const uint64_t dK0 = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
       const uint64_t dV0 = make_sdesc_sw128(smem_u32(sKV + kTileBytes), BT * 128, 1024);
       auto issue_S = [&](int j) {                // S_{j} into buffer j & 1 from stage j % NS
         const uint64_t dk = sdesc_add(dK0, (j % NS) * 2 * kTileBytes);
+        if constexpr (kF8) {
+          // S = K (sum of the query parts)^T: four K = 32 steps per part
 #pragma unroll
-        for (int kk = 0; kk < kDim / 16; ++kk) {
-          const uint32_t offk = (kk >> 2) * (BT * 128) + (kk & 3) * 32;
-          const uint32_t offq = (kk >> 2) * C::kBlock + (kk & 3) * 32;
-          mma_ss(tmem + (j & 1) * NP, sdesc_add(dk, offk), sdesc_add(dQ, offq), idS, kk > 0);
+          for (int part = 0; part < kParts; ++part)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ss_f8(tmem + (j & 1) * NP, sdesc_add(dk, kk * 32), sdesc_add(dQ, part * C::kBlock + kk * 32), idS,
+                        (part > 0 || kk > 0));
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < kDim / 16; ++kk) {
+            const uint32_t offk = (kk >> 2) * (BT * 128) + (kk & 3) * 32;
+            const uint32_t offq = (kk >> 2) * C::kBlock + (kk & 3) * 32;
+            mma_ss(tmem + (j & 1) * NP, sdesc_add(dk, offk), sdesc_add(dQ, offq), idS, kk > 0);
+          }
         }
         mma_commit(bSf + (j & 1));
       };
@@ -244,10 +349,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint64_t dv = sdesc_add(dV0, (jp % NS) * 2 * kTileBytes);
           const uint64_t dp = sdesc_add(dP0, (jp & 1) * C::kPBytes);
+          if constexpr (kF8) {
+            // O^T += V^T (sum of the P parts)^T: the V tile read MN-major (d = M,
+            // one 128-byte block), 32 cache rows per step
 #pragma unroll
-          for (int kk = 0; kk < BT / 16; ++kk) {
-            const uint32_t offp = (kk >> 2) * C::kBlock + (kk & 3) * 32;
-            mma_ss(tmem + col_o, sdesc_add(dv, kk * 16 * 128), sdesc_add(dp, offp), idO, (jp > 0 || kk > 0));
+            for (int part = 0; part < kParts; ++part)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_ss_f8(tmem + col_o + part * NP, sdesc_add(dv, kk * 32 * 128),
+                          sdesc_add(dp, part * C::kBlock + kk * 32), idO, (jp > 0 || kk > 0));
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < BT / 16; ++kk) {
+              const uint32_t offp = (kk >> 2) * C::kBlock + (kk & 3) * 32;
+              mma_ss(tmem + col_o, sdesc_add(dv, kk * 16 * 128), sdesc_add(dp, offp), idO, (jp > 0 || kk > 0));
+            }
           }
           mma_commit(bPfree + (jp & 1));
           mma_commit(bEmpty + jp % NS);
@@ -281,6 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int kb = tid >> 6, kc = tid & 63;       // this row's place in a Pᵀ row
     const uint32_t p_off = kb * C::kBlock + (kc & 7) * 2;
+    float qf[NP];                                 // fp8: undoes the per-head query scale
+#pragma unroll
+    for (int h = 0; h < NP; ++h) qf[h] = kF8 ? s_qinv[h] * p.scale_log2 : p.scale_log2;
     for (int j = 0; j < n_tiles; ++j) {
       const int buf = j & 1;
       mbar_wait(bSf + buf, (j >> 1) & 1, abort_flag, kSiteDecodeTc);
@@ -296,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool up = false;
 #pragma unroll
       for (int h = 0; h < NP; ++h) {
-        s[h] = valid ? __uint_as_float(r[h]) * p.scale_log2 : -INFINITY;
+        s[h] = valid ? __uint_as_float(r[h]) * qf[h] : -INFINITY;
         if (h < G) up |= s[h] > m_run[h] + kRescaleLog2;
       }
       if (bar_any_named(1, 128, up)) {
@@ -328,13 +447,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(bPfree + ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, kSiteDecodeTc);
           __syncwarp();
           tc_fence_after();
-          uint32_t ov[NP];
-          tmem_ld_np<NP>(tmem + lane_base + col_o, ov);
-          tmem_wait_ld();
-          reg_fence(ov);
 #pragma unroll
-          for (int h = 0; h < NP; ++h) ov[h] = __float_as_uint(__uint_as_float(ov[h]) * alpha[h]);
-          tmem_st_np<NP>(tmem + lane_base + col_o, ov);
+          for (int part = 0; part < (kF8 ? kParts : 1); ++part) {
+            uint32_t ov[NP];
+            tmem_ld_np<NP>(tmem + lane_base + col_o + part * NP, ov);
+            tmem_wait_ld();
+            reg_fence(ov);
+#pragma unroll
+            for (int h = 0; h < NP; ++h) ov[h] = __float_as_uint(__uint_as_float(ov[h]) * alpha[h]);
+            tmem_st_np<NP>(tmem + lane_base + col_o + part * NP, ov);
+          }
           tmem_wait_st();
         }
       }
@@ -343,20 +465,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(bFull + j % NS, (j / NS) & 1, abort_flag, kSiteDecodeTc);
         uint8_t* vrow = sKV + (j % NS) * 2 * kTileBytes + kTileBytes + tid * 128;
 #pragma unroll
-        for (int cb = 0; cb < 2; ++cb)
+        for (int cb = 0; cb < (kF8 ? 1 : 2); ++cb)
 #pragma unroll
           for (int c = 0; c < 8; ++c)
             reinterpret_cast<uint4*>(vrow + cb * BT * 128)[c] = make_uint4(0u, 0u, 0u, 0u);
       }
       // P_j into buffer `buf` once P_{j-2}·V_{j-2} has read it
       if (j >= 2) mbar_wait(bPfree + buf, ((j - 2) >> 1) & 1, abort_flag, kSiteDecodeTc);
-      uint8_t* pb = sP + buf * C::kPBytes + p_off;
+      if constexpr (kF8) {
+        // P (<= 2^8) as kParts e4m3 parts; row h of each part, byte `tid` of
+        // that row (128-byte swizzle)
+        uint8_t* pb = sP + buf * C::kPBytes + (tid & 15);
+        const int chunk = tid >> 4;
 #pragma unroll
-      for (int h = 0; h < NP; ++h) {
-        if (h >= G) break;
-        const float pr = ex2(s[h] - m_run[h]);     // 0 for masked rows
-        l_part[h] += pr;
-        *reinterpret_cast<uint16_t*>(pb + h * 128 + (((kc >> 3) ^ (h & 7)) << 4)) = to16<T>(pr);
+        for (int h = 0; h < NP; h += 2) {
+          if (h >= G) break;
+          const float p0 = ex2(s[h] - m_run[h]);   // 0 for masked rows
+          const float p1 = (h + 1 < G) ? ex2(s[h + 1] - m_run[h + 1]) : 0.f;
+          l_part[h] += p0;
+          if (h + 1 < G) l_part[h + 1] += p1;
+          uint16_t pr[kParts];
+          split_e4m3<true>(p0, p1, pr);
+          const int o0 = h * 128 + ((chunk ^ (h & 7)) << 4), o1 = (h + 1) * 128 + ((chunk ^ ((h + 1) & 7)) << 4);
+#pragma unroll
+          for (int k = 0; k < kParts; ++k) {
+            pb[k * C::kBlock + o0] = (uint8_t)(pr[k] & 0xff);
+            pb[k * C::kBlock + o1] = (uint8_t)(pr[k] >> 8);
+          }
+        }
+      } else {
+        uint8_t* pb = sP + buf * C::kPBytes + p_off;
+#pragma unroll
+        for (int h = 0; h < NP; ++h) {
+          if (h >= G) break;
+          const float pr = ex2(s[h] - m_run[h]);     // 0 for masked rows
+          l_part[h] += pr;
+          *reinterpret_cast<uint16_t*>(pb + h * 128 + (((kc >> 3) ^ (h & 7)) << 4)) = to16<T>(pr);
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -372,12 +517,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bPfree + ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, abort_flag, kSiteDecodeTc);
       __syncwarp();
       tc_fence_after();
-      uint32_t ov[NP];
-      tmem_ld_np<NP>(tmem + lane_base + col_o, ov);
-      tmem_wait_ld();
-      reg_fence(ov);
+      float w = 1.f;
 #pragma unroll
-      for (int h = 0; h < NP; ++h) o[h] = __uint_as_float(ov[h]);
+      for (int part = 0; part < (kF8 ? kParts : 1); ++part, w *= 1.f / kPartScale) {
+        uint32_t ov[NP];
+        tmem_ld_np<NP>(tmem + lane_base + col_o + part * NP, ov);
+        tmem_wait_ld();
+        reg_fence(ov);
+#pragma unroll
+        for (int h = 0; h < NP; ++h) o[h] = fmaf(__uint_as_float(ov[h]), w, o[h]);
+      }
     }
 #pragma unroll
     for (int h = 0; h < NP; ++h) {
@@ -487,13 +636,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) p.ws_count[bkv * n_slices + slice] = 0;  // leave the workspace zeroed for the next call
 }
 
-// The tensor-core kernel takes D = 128, q and cache of the same 16-bit type
-// and G >= 2.
+// The tensor-core kernel takes D = 128 and either q and cache of the same
+// 16-bit type with G >= 2, or an e4m3 cache (any G) with f16 / bf16 queries.
 constexpr int kSliceHeads = 16;   // query heads per CTA (the MMA's N)
 
 inline bool tc_eligible(long long H, long long H_kv, long long D, int q_dtype, int kv_dtype) {
-  return D == kDim && q_dtype == kv_dtype && (kv_dtype == PU_DTYPE_F16 || kv_dtype == PU_DTYPE_BF16) &&
-         H / H_kv >= 2;
+  if (D != kDim) return false;
+  if (kv_dtype == PU_DTYPE_FP8_E4M3) return q_dtype == PU_DTYPE_F16 || q_dtype == PU_DTYPE_BF16;
+  return q_dtype == kv_dtype && (kv_dtype == PU_DTYPE_F16 || kv_dtype == PU_DTYPE_BF16) && H / H_kv >= 2;
 }
 
 inline long long n_slices(long long G) { return (G + kSliceHeads - 1) / kSliceHeads; }
@@ -506,10 +656,11 @@ constexpr long long kMaxRecords = 256;
 // One CTA per SM; chunks are whole tiles; at most kMaxRecords / (heads of a
 // slice) splits (the merge weights, heads x splits floats, fit in the idle
 // K/V ring).
-inline Plan tc_plan(long long B, long long H, long long H_kv, long long n, int num_sms, bool ragged) {
+inline Plan tc_plan(long long B, long long H, long long H_kv, long long n, int num_sms, bool ragged,
+                    int ctas_per_sm = 1) {
   const long long G = H / H_kv;
-  Plan pl = make_plan(B * H_kv * n_slices(G), n, kDim, num_sms / kCtasPerSm > 0 ? num_sms / kCtasPerSm : 1,
-                      ragged, BT);
+  const int slots = num_sms * ctas_per_sm / kCtasPerSm;     // make_plan counts kCtasPerSm CTAs per SM
+  Plan pl = make_plan(B * H_kv * n_slices(G), n, kDim, slots > 0 ? slots : 1, ragged, BT);
   const long long cap = std::max<long long>(1, kMaxRecords / std::min<long long>(G, kSliceHeads));
   if (pl.splits > cap) {
     const long long chunk = ((n + cap - 1) / cap + BT - 1) / BT * BT;
@@ -520,26 +671,35 @@ inline Plan tc_plan(long long B, long long H, long long H_kv, long long n, int n
   return pl;
 }
 
-template <typename T, int NP>
+template <typename T, typename KVT, int NP>
 int launch_np(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, dim3 grid, cudaStream_t st) {
-  constexpr int smem = Cfg<NP>::kSmemBytes;
-  const int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(gqa_tc_kernel<T, NP>), smem,
+  constexpr int smem = Cfg<NP, KVT>::kSmemBytes;
+  const int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(gqa_tc_kernel<T, KVT, NP>), smem,
                                       "grouped-head decode (tensor core) shared memory");
   if (rc) return rc;
-  gqa_tc_kernel<T, NP><<<grid, kThreads, smem, st>>>(tk, tv, prm);
+  gqa_tc_kernel<T, KVT, NP><<<grid, kThreads, smem, st>>>(tk, tv, prm);
   return check_cuda(cudaGetLastError(), "grouped-head decode (tensor core) launch");
 }
 
-inline int launch(const Params& prm, int kv_dtype, long long B, long long H_kv, cudaStream_t st) {
-  if ((long long)kSliceHeads * prm.splits + 2 * kSliceHeads > NS * 2 * kTileBytes / 4)
+inline int launch(const Params& prm, int q_dtype, int kv_dtype, long long B, long long H_kv, cudaStream_t st) {
+  const bool f8 = kv_dtype == PU_DTYPE_FP8_E4M3;
+  const long long ring = f8 ? (long long)Ring<__nv_fp8_e4m3>::NS * 2 * Ring<__nv_fp8_e4m3>::kTileBytes
+                            : (long long)Ring<__half>::NS * 2 * Ring<__half>::kTileBytes;
+  if ((long long)kSliceHeads * prm.splits + 2 * kSliceHeads > ring / 4)
     return set_error(PU_ERR_UNSUPPORTED, "grouped-head decode: %d splits exceed the merge space", prm.splits);
   CUtensorMap tk, tv;
-  int rc = make_tmap_bf16_3d(&tk, prm.k, kDim, prm.n_local, B * H_kv, 64, BT, true);
-  if (!rc) rc = make_tmap_bf16_3d(&tv, prm.v, kDim, prm.n_local, B * H_kv, 64, BT, true);
+  int rc = f8 ? make_tmap_u8_3d(&tk, prm.k, kDim, prm.n_local, B * H_kv, kDim, BT, true)
+              : make_tmap_bf16_3d(&tk, prm.k, kDim, prm.n_local, B * H_kv, 64, BT, true);
+  if (!rc)
+    rc = f8 ? make_tmap_u8_3d(&tv, prm.v, kDim, prm.n_local, B * H_kv, kDim, BT, true)
+            : make_tmap_bf16_3d(&tv, prm.v, kDim, prm.n_local, B * H_kv, 64, BT, true);
   if (rc) return rc;
   const dim3 grid((unsigned)(prm.splits * n_slices(prm.group)), (unsigned)(B * H_kv));
-  return kv_dtype == PU_DTYPE_F16 ? launch_np<__half, kSliceHeads>(tk, tv, prm, grid, st)
-                                  : launch_np<__nv_bfloat16, kSliceHeads>(tk, tv, prm, grid, st);
+  if (f8)
+    return q_dtype == PU_DTYPE_F16 ? launch_np<__half, __nv_fp8_e4m3, kSliceHeads>(tk, tv, prm, grid, st)
+                                   : launch_np<__nv_bfloat16, __nv_fp8_e4m3, kSliceHeads>(tk, tv, prm, grid, st);
+  return kv_dtype == PU_DTYPE_F16 ? launch_np<__half, __half, kSliceHeads>(tk, tv, prm, grid, st)
+                                  : launch_np<__nv_bfloat16, __nv_bfloat16, kSliceHeads>(tk, tv, prm, grid, st);
 }
 
 }  // namespace tc
@@ -558,6 +718,9 @@ size_t pu_decode_gqa_workspace_size(int64_t B, int64_t H, int64_t H_kv, int64_t 
   if (gqa_grouped(H, H_kv))
     bytes = std::max({bytes, gqa_plan(B, H, H_kv, n, D, sms, false).total_bytes,
                       gqa_plan(B, H, H_kv, n, D, sms, true).total_bytes});
+  if (tc::tc_eligible(H, H_kv, D, PU_DTYPE_F16, PU_DTYPE_FP8_E4M3))
+    bytes = std::max({bytes, tc::tc_plan(B, H, H_kv, n, sms, false, tc::kF8CtasPerSm).total_bytes,
+                      tc::tc_plan(B, H, H_kv, n, sms, true, tc::kF8CtasPerSm).total_bytes});
   if (tc::tc_eligible(H, H_kv, D, PU_DTYPE_F16, PU_DTYPE_F16))
     bytes = std::max({bytes, tc::tc_plan(B, H, H_kv, n, sms, false).total_bytes,
                       tc::tc_plan(B, H, H_kv, n, sms, true).total_bytes});
@@ -577,13 +740,14 @@ int pu_decode_gqa(const void* q, int q_dtype, const void* k_cache, const void* v
                          (long long)H_kv);
   if (!(k_scale > 0.f) || !(v_scale > 0.f) || !isfinite(k_scale) || !isfinite(v_scale))
     return pu::set_error(PU_ERR_INVALID_ARGUMENT, "k_scale and v_scale must be positive and finite");
-  // tensor core for 16-bit caches with D = 128 and 2 <= G <= 32; the
-  // CUDA-core grouped kernel for fp8 caches, D = 64 or mixed dtypes (G = 2,
-  // 4, 8); otherwise the query-head kernel reading K/V head h / G
+  // tensor core for D = 128 with 16-bit caches and G >= 2 or e4m3 caches
+  // and any G; the CUDA-core grouped kernel for D = 64 or mixed 16-bit
+  // dtypes (G = 2, 4, 8); otherwise the query-head kernel reading K/V head h / G
   const bool on_tc = tc::tc_eligible(H, H_kv, D, q_dtype, kv_dtype);
   const bool grouped = !on_tc && gqa_grouped(H, H_kv);
   const bool ragged = kv_lens != nullptr;
-  const Plan pl = on_tc ? tc::tc_plan(B, H, H_kv, n, pu::sm_count(), ragged)
+  const Plan pl = on_tc ? tc::tc_plan(B, H, H_kv, n, pu::sm_count(), ragged,
+                                      kv_dtype == PU_DTYPE_FP8_E4M3 ? tc::kF8CtasPerSm : 1)
                         : grouped ? gqa_plan(B, H, H_kv, n, D, pu::sm_count(), ragged)
                                   : make_plan(B * H, n, D, pu::sm_count(), ragged);
   if (!workspace || workspace_bytes < pl.total_bytes)
@@ -606,7 +770,7 @@ int pu_decode_gqa(const void* q, int q_dtype, const void* k_cache, const void* v
   prm.ws_count = static_cast<int*>(workspace);
   prm.o = static_cast<__nv_bfloat16*>(o);
   prm.lse = lse;
-  if (on_tc) return tc::launch(prm, kv_dtype, B, H_kv, static_cast<cudaStream_t>(stream));
+  if (on_tc) return tc::launch(prm, q_dtype, kv_dtype, B, H_kv, static_cast<cudaStream_t>(stream));
   if (grouped)
     return launch_gqa(prm, q_dtype, kv_dtype, (int)D, prm.group, (int)(B * H_kv), static_cast<cudaStream_t>(stream));
   return launch<true>(prm, q_dtype, kv_dtype, (int)D, (int)(B * H), static_cast<cudaStream_t>(stream));

@@ -19,6 +19,10 @@ namespace pu {
 int make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
                       uint64_t outer, uint32_t box_cols, uint32_t box_rows, bool swizzle128);
 
+// Same for 8-bit elements (fp8 caches).
+int make_tmap_u8_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t outer,
+                    uint32_t box_cols, uint32_t box_rows, bool swizzle128);
+
 // Same for fp32 elements (used for the dQ accumulator).
 int make_tmap_f32_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
                      uint64_t outer, uint32_t box_cols, uint32_t box_rows, bool swizzle128);

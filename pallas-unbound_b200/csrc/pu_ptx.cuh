@@ -311,6 +311,17 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem] with 8-bit (e4m3) operands.
+__device__ __forceinline__ void mma_ss_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive (once) on an mbarrier when all previously issued tcgen05.mma of
 // this thread have completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -424,6 +435,14 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, int a_mn_ma
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
          (static_cast<uint32_t>(b_mn_major) << 16) | ((static_cast<uint32_t>(N) >> 3) << 17) |
          ((static_cast<uint32_t>(M) >> 4) << 24);
+}
+
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B (format code 0),
+// fp32 accumulate; the fields are those of make_idesc_bf16.  One MMA covers
+// K = 32 elements (32 bytes of a 128-byte swizzle row).
+__host__ __device__ constexpr uint32_t make_idesc_e4m3(int M, int N, int a_mn_major, int b_mn_major) {
+  return (1u << 4) | (static_cast<uint32_t>(a_mn_major) << 15) | (static_cast<uint32_t>(b_mn_major) << 16) |
+         ((static_cast<uint32_t>(N) >> 3) << 17) | ((static_cast<uint32_t>(M) >> 4) << 24);
 }
 
 // Same for either 16-bit input type (`bf16` false: f16 A and B).
