@@ -577,13 +577,15 @@ def bench_decode(steps: int, warmup: int, rank: int, world: int, transport: str 
         times.append(e0.elapsed_time(e1))
     # steady state: `steps` steps back to back under one pair of events, each
     # step on the next of R cache copies, R * shard > 2 x L2, so no step finds
-    # its shard in L2 (no flush, no per-step launch gap)
+    # its shard in L2 (no flush, no per-step launch gap), the host ahead of
+    # the device
     copies = max(1, -(-2 * L2_BYTES // (2 * k.numel() * k.element_size())))
     ring = [(k, v)] + [(k.clone(), v.clone()) for _ in range(copies - 1)]
     for i in range(warmup):
         dec.pallas_flash_decoding(q, *ring[i % copies], group=group, transport=transport)
     torch.cuda.synchronize()
     barrier(world)
+    gpu_lead(steps)
     device_align(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -605,6 +607,7 @@ def bench_decode(steps: int, warmup: int, rank: int, world: int, transport: str 
     for i in range(warmup):
         local(i)
     torch.cuda.synchronize()
+    gpu_lead(steps)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(steps):
@@ -665,15 +668,32 @@ def _timed(fn, steps, flush, stream, world: int = 1):
     return statistics.median(times) * 1e3
 
 
+_LEAD = {}
+
+
+def gpu_lead(steps: int):
+    """Queues about 0.3 ms of device work (L2 flushes) per 6 steps ahead of a
+    back-to-back timed loop, so the host has enqueued the steps before the
+    device reaches them: the events then time device work only, for steps
+    whose host-side call (~30 us) is as long as their device time."""
+    f = _LEAD.get("flush")
+    if f is None:
+        f = _LEAD["flush"] = L2Flush()
+    for _ in range(max(1, -(-steps // 6))):
+        f()
+
+
 def _steady(fn, ring, steps: int, warmup: int, stream, world: int = 1) -> float:
     """Microseconds per call of `steps` calls back to back under one pair of
     CUDA events, call i on ring[i % len(ring)] (the caller sizes the ring so
-    its inputs exceed twice the L2: no call finds its inputs there)."""
+    its inputs exceed twice the L2: no call finds its inputs there), with
+    the host ahead of the device (gpu_lead)."""
     import torch
     for i in range(warmup):
         fn(ring[i % len(ring)])
     torch.cuda.synchronize()
     barrier(world)
+    gpu_lead(steps)
     device_align(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -767,7 +787,11 @@ def bench_outproj(steps: int, warmup: int, rank: int, world: int):
     """Attention output projection + TP all-reduce: every rank multiplies its
     16 heads' output [16384, 2048] by its rows of W_O [2048, 2048]; the
     partial products are summed over the ranks (weak scaling: K per rank is
-    fixed).  Returns {transport: us} (max over ranks)."""
+    fixed).  Returns {transport: (us, latency_us, copies)} (max over ranks):
+    us per call of `steps` calls back to back under one pair of events, call
+    i reading copy i mod R of the activation (R copies exceed twice the L2);
+    latency_us the median of single calls, each started on an idle GPU (so
+    it includes the host-side work before the launch)."""
     import torch
     from pallas_flash.distributed.outproj import out_proj_all_reduce
 
@@ -783,14 +807,15 @@ def bench_outproj(steps: int, warmup: int, rank: int, world: int):
     else:
         group = single_rank_group()
     stream = torch.cuda.current_stream()
+    ring = [o] + [o.clone() for _ in range(_copies(o.numel() * o.element_size()) - 1)]
     out = {}
     for transport in ("peer", "nccl"):
         if world == 1 and transport == "nccl":
-            fn = lambda: torch.matmul(o, w, out=y)
+            fn = lambda a: torch.matmul(a, w, out=y)
         else:
-            fn = lambda: out_proj_all_reduce(o, w, group, transport=transport, out=y)
+            fn = lambda a: out_proj_all_reduce(a, w, group, transport=transport, out=y)
         for _ in range(warmup):
-            fn()
+            fn(o)
         torch.cuda.synchronize()
         barrier(world)
         times = []
@@ -799,11 +824,14 @@ def bench_outproj(steps: int, warmup: int, rank: int, world: int):
             device_align(world)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            fn()
+            fn(o)
             e1.record(stream)
             torch.cuda.synchronize()
             times.append(e0.elapsed_time(e1))
-        out[transport] = allreduce_max(statistics.median(times) * 1e3, world)
+        lat = allreduce_max(statistics.median(times) * 1e3, world)
+        us = allreduce_max(_steady(fn, ring, max(steps, len(ring)), warmup, stream, world), world)
+        out[transport] = (us, lat, len(ring))
+    del ring
     return out
 
 
@@ -921,7 +949,7 @@ def main():
         return
     if args.profile_leg == "outproj":
         op = bench_outproj(args.steps, warmup, rank, world)
-        print(f"out-projection leg: {op['peer']:.1f} us/step", flush=True)
+        print(f"out-projection leg: {op['peer'][0]:.1f} us/step", flush=True)
         return
     parity = run_parity(rank, world) if args.profile_leg is None else None
     clocks = ClockSampler(local).start()
@@ -1000,7 +1028,8 @@ def main():
                        "frac_aggregate_hbm": round(dec_total_bytes / (dec_steady * 1e-6) / 1e9 /
                                                    (peaks["hbm_gbs"] * world), 4),
                        "timing": f"{dec_steps} steps back to back over {dec_copies} cache copies "
-                                 "(each step's shard out of L2), one pair of CUDA events",
+                                 "(each step's shard out of L2), one pair of CUDA events, the host "
+                                 "ahead of the device (steps enqueued before the first event fires)",
                        "latency_us": round(dec_us, 2),
                        "latency_timing": "one step between CUDA events after a 1 GiB L2 flush, median "
                                          "(includes ~6-7 us of launch gap: a one-element kernel reads "
@@ -1033,13 +1062,19 @@ def main():
         line["outproj"] = {
             "workload": f"out-projection + TP all-reduce: per rank [{OP_T}, {OP_K}] x [{OP_K}, {OP_N}] bf16, "
                         f"partials summed over {world} GPU(s), result on every rank",
-            "fused_peer_us": round(op["peer"], 2),
-            ("matmul_nccl_allreduce_us" if world > 1 else "cublas_matmul_us"): round(op["nccl"], 2),
-            "gemm_TFLOP_s_per_gpu": round(op_flops / (op["peer"] * 1e-6) / 1e12, 1),
+            "timing": f"*_us: calls back to back over {op['peer'][2]} copies of the activation (out of "
+                      "L2), one pair of CUDA events; *_latency_us: median single call started on an "
+                      "idle GPU (includes the host-side work before the launch)",
+            "fused_peer_us": round(op["peer"][0], 2),
+            ("matmul_nccl_allreduce_us" if world > 1 else "cublas_matmul_us"): round(op["nccl"][0], 2),
+            "fused_peer_latency_us": round(op["peer"][1], 2),
+            ("matmul_nccl_allreduce_latency_us" if world > 1 else "cublas_matmul_latency_us"):
+                round(op["nccl"][1], 2),
+            "gemm_TFLOP_s_per_gpu": round(op_flops / (op["peer"][0] * 1e-6) / 1e12, 1),
             "nvlink_bytes_out_per_gpu": link_bytes,
             "roofline": {"bound": "tensor" if world == 1 else "max(tensor, nvlink)",
                          "floor_us": round(op_floor_us, 2),
-                         "frac": round(op_floor_us / op["peer"], 4),
+                         "frac": round(op_floor_us / op["peer"][0], 4),
                          "peaks": f"{peaks['bf16_tflops']} TFLOP/s bf16 (measured), 770 GB/s NVLink per "
                                   "direction (measured peer copy)"}}
         if long_ms:

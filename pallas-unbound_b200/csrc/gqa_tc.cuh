@@ -32,10 +32,18 @@
 //                  thread; at the end thread d reads row d of Oᵀ and the
 //                  split record of every head is written
 //   all            the last CTA of a (b, K/V head, slice) merges the split
-//                  records of its heads at once (weights in the idle ring)
+//                  records of its heads at once, 32 records per L2 round trip
 //
-// TMEM (64 columns): S_0 [0,16), S_1 [16,32), Oᵀ [32,48); e4m3 caches: Oᵀ of
-// each P part at [32 + 16 k, 48 + 16 k) (128 columns allocated).
+// The launch allows programmatic dependent launch: the first global access
+// of every CTA follows grid_dep_wait, so the CTAs may be placed on SMs as
+// the previous kernel's CTAs leave, and the barriers, TMEM and the first
+// ring of K/V loads are set up before the queries arrive.
+//
+// TMEM (64 columns): S_0 [0,16), S_1 [16,32), Oᵀ [32,48).  e4m3 caches (256
+// columns): S_0 [0,48) and S_1 [48,96), each the scores of the three query
+// parts side by side, and Oᵀ of P part k at [96 + 16 k, 112 + 16 k); the
+// products run with N = 48 over the three parts stacked in shared memory
+// (one instruction where three N = 16 ones would cost three times the issue).
 // Rows past the chunk's end inside the last tile are masked to -inf; their V
 // rows are zeroed in shared memory before the P·V product (so stale cache
 // contents cannot reach the output).  Every wait is bounded; the softmax
@@ -57,6 +65,7 @@ constexpr int kDim = 128;                  // head size
 constexpr int NS = 3;                      // K/V ring depth
 constexpr int kTileBytes = BT * kDim * 2;  // one K or V tile
 constexpr float kRescaleLog2 = 8.f;
+constexpr int kMergeBatch = 32;            // split records per L2 round trip of the merge
 static_assert(kThreads == 256, "the softmax warps are 0-3, producer 4, issuer 5");
 
 // Cache tiles of one element type: 16-bit tiles are two 64-column swizzle
@@ -96,8 +105,14 @@ struct Cfg {
   static constexpr int kOffQinv = kOffRed + 4 * NP * 4;    // fp8: [NP] per-head factor undoing the query scale
   static constexpr int kSmemBytes = kOffQinv + NP * 4;
   // S_0, S_1, then one O^T accumulator (16-bit) or kParts of them (e4m3: one
-  // per P part, combined with weights kPartScale^-part at the end)
-  static constexpr uint32_t kTmemCols = (NP <= 16 && sizeof(KVT) == 2) ? 64 : 128;
+  // per P part, combined with weights kPartScale^-part at the end).  e4m3:
+  // each S buffer holds the scores of the kParts query parts side by side
+  // (kParts x NP columns, summed by the softmax warps), and the products run
+  // with N = kParts x NP over the parts stacked in shared memory.
+  static constexpr int kSCols = (sizeof(KVT) == 1 ? kParts : 1) * NP;
+  static constexpr uint32_t kColO = 2 * kSCols;
+  static constexpr uint32_t kTmemCols = sizeof(KVT) == 1 ? 256 : (NP <= 16 ? 64 : 128);
+  static_assert(kColO + (sizeof(KVT) == 1 ? kParts : 1) * NP <= kTmemCols, "TMEM columns");
   static_assert(kOffP % 1024 == 0 && kPBytes % 1024 == 0 && kOffKV % 1024 == 0,
                 "swizzled operands start on 1024-byte boundaries");
 };
@@ -202,6 +217,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t_end = min(t_begin + p.chunk, len);
   const int n_tiles = t_end > t_begin ? (t_end - t_begin + BT - 1) / BT : 0;
 
+  // The producer sets up the barriers and puts the first ring of K/V loads
+  // in flight before anything else, so the first tiles travel while the
+  // queries are staged.  Nothing in global memory (q, the cache, the lengths
+  // or the workspace) is touched before grid_dep_wait: the launch may begin
+  // while the previous kernel of the stream is still finishing.
+  constexpr int kProducer = 4 * 32;
+  if (tid == kProducer) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bFull + s, 1);
+      mbar_init(bEmpty + s, 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bSf + t, 1);
+      mbar_init(bPf + t, 128);
+      mbar_init(bPfree + t, 1);
+    }
+    mbar_init(bDrain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  grid_dep_wait();
+  grid_dep_launch_dependents();
+  const int n_first = min(NS, n_tiles);
+  auto issue_tile = [&](int i) {
+    const int s = i % NS;
+    uint8_t* dK = sKV + s * 2 * kTileBytes;
+    uint8_t* dV = dK + kTileBytes;
+    const int row = t_begin + i * BT;
+    mbar_arrive_expect_tx(bFull + s, 2 * kTileBytes);
+    if constexpr (kF8) {
+      tma_load_3d(dK, &tmK, bFull + s, 0, row, bkv);
+      tma_load_3d(dV, &tmV, bFull + s, 0, row, bkv);
+    } else {
+      for (int cb = 0; cb < 2; ++cb) tma_load_3d(dK + cb * BT * 128, &tmK, bFull + s, cb * 64, row, bkv);
+      for (int cb = 0; cb < 2; ++cb) tma_load_3d(dV + cb * BT * 128, &tmV, bFull + s, cb * 64, row, bkv);
+    }
+  };
+  if (tid == kProducer) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    for (int i = 0; i < n_first; ++i) issue_tile(i);
+  }
+
   // query group -> sQ (K-major, 128-byte swizzle; rows G..NP-1 zero); both
   // Pᵀ buffers zeroed (rows G..NP-1 are never written afterwards)
   float* s_qinv = reinterpret_cast<float*>(smem + C::kOffQinv);
@@ -249,51 +311,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int c = tid; c < 2 * C::kPBytes / 16; c += kThreads)
     reinterpret_cast<uint4*>(sP)[c] = make_uint4(0u, 0u, 0u, 0u);
   fence_proxy_async_smem();
-  if (tid == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(bFull + s, 1);
-      mbar_init(bEmpty + s, 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(bSf + t, 1);
-      mbar_init(bPf + t, 128);
-      mbar_init(bPfree + t, 1);
-    }
-    mbar_init(bDrain, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
-    tmem_relinquish();
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t col_o = 2 * NP;
+  const uint32_t col_o = C::kColO;
 
   if (warp == 4) {
     // ---------------- TMA producer ----------------
     if (lane == 0 && n_tiles > 0) {
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      int issued = 0;
-      for (int i = 0; i < n_tiles; ++i) {
-        const int s = i % NS;
-        const int u = i / NS;
-        if (u > 0 && !mbar_wait(bEmpty + s, (u - 1) & 1, abort_flag, kSiteDecodeTc)) break;
-        uint8_t* dK = sKV + s * 2 * kTileBytes;
-        uint8_t* dV = dK + kTileBytes;
-        const int row = t_begin + i * BT;
-        mbar_arrive_expect_tx(bFull + s, 2 * kTileBytes);
-        if constexpr (kF8) {
-          tma_load_3d(dK, &tmK, bFull + s, 0, row, bkv);
-          tma_load_3d(dV, &tmV, bFull + s, 0, row, bkv);
-        } else {
-          for (int cb = 0; cb < 2; ++cb) tma_load_3d(dK + cb * BT * 128, &tmK, bFull + s, cb * 64, row, bkv);
-          for (int cb = 0; cb < 2; ++cb) tma_load_3d(dV + cb * BT * 128, &tmV, bFull + s, cb * 64, row, bkv);
-        }
+      int issued = n_first;                     // the first ring went out in the prologue
+      for (int i = n_first; i < n_tiles; ++i) {
+        if (!mbar_wait(bEmpty + i % NS, (i / NS - 1) & 1, abort_flag, kSiteDecodeTc)) break;
+        issue_tile(i);
         ++issued;
       }
       // copies still in flight land before the CTA may exit
@@ -305,8 +335,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- tcgen05 issuer ----------------
     if (lane == 0) {
       constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-      constexpr uint32_t idS = kF8 ? make_idesc_e4m3(BT, NP, 0, 0) : make_idesc_16(BT, NP, 0, 0, kBf16);
-      constexpr uint32_t idO = kF8 ? make_idesc_e4m3(kDim, NP, 1, 0) : make_idesc_16(kDim, NP, 1, 0, kBf16);
+      constexpr uint32_t idS = kF8 ? make_idesc_e4m3(BT, kParts * NP, 0, 0) : make_idesc_16(BT, NP, 0, 0, kBf16);
+      constexpr uint32_t idO = kF8 ? make_idesc_e4m3(kDim, kParts * NP, 1, 0) : make_idesc_16(kDim, NP, 1, 0, kBf16);
       const uint64_t dQ = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t dP0 = make_sdesc_sw128(smem_u32(sP), 16, 1024);
       const uint64_t dK0 = make_sdesc_sw128(smem_u32(sKV), 16, 1024);
@@ -314,19 +344,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_S = [&](int j) {                // S_{j} into buffer j & 1 from stage j % NS
         const uint64_t dk = sdesc_add(dK0, (j % NS) * 2 * kTileBytes);
         if constexpr (kF8) {
-          // S = K (sum of the query parts)^T: four K = 32 steps per part
+          // [S_part0 | S_part1 | S_part2] = K (query parts stacked, N = kParts x NP)^T:
+          // four K = 32 steps
 #pragma unroll
-          for (int part = 0; part < kParts; ++part)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_ss_f8(tmem + (j & 1) * NP, sdesc_add(dk, kk * 32), sdesc_add(dQ, part * C::kBlock + kk * 32), idS,
-                        (part > 0 || kk > 0));
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ss_f8(tmem + (j & 1) * C::kSCols, sdesc_add(dk, kk * 32), sdesc_add(dQ, kk * 32), idS, kk > 0);
         } else {
 #pragma unroll
           for (int kk = 0; kk < kDim / 16; ++kk) {
             const uint32_t offk = (kk >> 2) * (BT * 128) + (kk & 3) * 32;
             const uint32_t offq = (kk >> 2) * C::kBlock + (kk & 3) * 32;
-            mma_ss(tmem + (j & 1) * NP, sdesc_add(dk, offk), sdesc_add(dQ, offq), idS, kk > 0);
+            mma_ss(tmem + (j & 1) * C::kSCols, sdesc_add(dk, offk), sdesc_add(dQ, offq), idS, kk > 0);
           }
         }
         mma_commit(bSf + (j & 1));
@@ -350,14 +378,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t dv = sdesc_add(dV0, (jp % NS) * 2 * kTileBytes);
           const uint64_t dp = sdesc_add(dP0, (jp & 1) * C::kPBytes);
           if constexpr (kF8) {
-            // O^T += V^T (sum of the P parts)^T: the V tile read MN-major (d = M,
-            // one 128-byte block), 32 cache rows per step
+            // [O_part0 | O_part1 | O_part2]^T += V^T (P parts stacked, N = kParts x
+            // NP)^T: the V tile read MN-major (d = M, one 128-byte block), 32
+            // cache rows per step
 #pragma unroll
-            for (int part = 0; part < kParts; ++part)
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_ss_f8(tmem + col_o + part * NP, sdesc_add(dv, kk * 32 * 128),
-                          sdesc_add(dp, part * C::kBlock + kk * 32), idO, (jp > 0 || kk > 0));
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ss_f8(tmem + col_o, sdesc_add(dv, kk * 32 * 128), sdesc_add(dp, kk * 32), idO, (jp > 0 || kk > 0));
           } else {
 #pragma unroll
             for (int kk = 0; kk < BT / 16; ++kk) {
@@ -405,17 +431,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bSf + buf, (j >> 1) & 1, abort_flag, kSiteDecodeTc);
       __syncwarp();
       tc_fence_after();
-      uint32_t r[NP];
-      tmem_ld_np<NP>(tmem + lane_base + buf * NP, r);
-      tmem_wait_ld();
-      reg_fence(r);
+      float raw[NP];
+      if constexpr (kF8) {
+        // the query parts' scores side by side: summed in part order
+        uint32_t r0[NP], r1[NP], r2[NP];
+        static_assert(kParts == 3, "three query parts");
+        tmem_ld_np<NP>(tmem + lane_base + buf * C::kSCols, r0);
+        tmem_ld_np<NP>(tmem + lane_base + buf * C::kSCols + NP, r1);
+        tmem_ld_np<NP>(tmem + lane_base + buf * C::kSCols + 2 * NP, r2);
+        tmem_wait_ld();
+        reg_fence(r0);
+        reg_fence(r1);
+        reg_fence(r2);
+#pragma unroll
+        for (int h = 0; h < NP; ++h)
+          raw[h] = (__uint_as_float(r0[h]) + __uint_as_float(r1[h])) + __uint_as_float(r2[h]);
+      } else {
+        uint32_t r[NP];
+        tmem_ld_np<NP>(tmem + lane_base + buf * C::kSCols, r);
+        tmem_wait_ld();
+        reg_fence(r);
+#pragma unroll
+        for (int h = 0; h < NP; ++h) raw[h] = __uint_as_float(r[h]);
+      }
       const int tile0 = t_begin + j * BT;
       const bool valid = tile0 + tid < t_end;
       float s[NP];
       bool up = false;
 #pragma unroll
       for (int h = 0; h < NP; ++h) {
-        s[h] = valid ? __uint_as_float(r[h]) * qf[h] : -INFINITY;
+        s[h] = valid ? raw[h] * qf[h] : -INFINITY;
         if (h < G) up |= s[h] > m_run[h] + kRescaleLog2;
       }
       if (bar_any_named(1, 128, up)) {
@@ -547,7 +592,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         rec[1] = (sm_red4[h] + sm_red4[NP + h]) + (sm_red4[2 * NP + h] + sm_red4[3 * NP + h]);
       }
     }
-    __threadfence();
   }
 
   tc_fence_before();
@@ -556,8 +600,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
-  __threadfence();
   if (tid == 0) {
+    // the barrier orders every thread's record stores before this fence, so
+    // one device-scope fence publishes the CTA's records before its count
+    __threadfence();
     const int prev = atomicAdd(p.ws_count + bkv * n_slices + slice, 1);
     *sm_last = (prev == p.splits - 1);
   }
@@ -565,73 +611,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!*sm_last) return;
   __threadfence();
   // last CTA of this (b, K/V head, slice): merge the split records of its G
-  // query heads at once (the records of heads bh0.. are contiguous); the K/V ring
-  // is idle now and holds the merge weights
+  // query heads.  Thread i takes outputs (h, d) and (h, d + 64) of head h =
+  // i / 64; it reads the records kMergeBatch at a time with every load of a
+  // batch in flight together (one L2 round trip per batch) and folds them,
+  // in record order, into a running maximum and running sums.
   const int S = p.splits;
   const float* recs = p.ws_rec + (size_t)bh0 * S * (kDim + 2);
-  float* sw = reinterpret_cast<float*>(sKV);    // [G][S]
-  float* sML = sw + G * S;                      // M [G], then L [G]
-  for (int h = warp; h < G; h += kWarps) {      // one warp per head
+  constexpr int kHalf = kDim / 2;
+  for (int pi = tid; pi < G * kHalf; pi += kThreads) {
+    const int h = pi / kHalf, d = pi % kHalf;
     const float* rh = recs + (size_t)h * S * (kDim + 2);
-    float mx = -INFINITY;
-    for (int s = lane; s < S; s += 32) mx = fmaxf(mx, __ldcg(rh + (size_t)s * (kDim + 2)));
+    float mx = -INFINITY, ls = 0.f, oa = 0.f, ob = 0.f;
+    for (int s0 = 0; s0 < S; s0 += kMergeBatch) {
+      float m[kMergeBatch], l[kMergeBatch], xa[kMergeBatch], xb[kMergeBatch];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float ls = 0.f;
-    for (int s = lane; s < S; s += 32) {
-      const float m = __ldcg(rh + (size_t)s * (kDim + 2));
-      const float w = (m == -INFINITY) ? 0.f : ex2(m - mx);   // every record empty: all 0
-      sw[h * S + s] = w;
-      ls += w * __ldcg(rh + (size_t)s * (kDim + 2) + 1);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-    if (lane == 0) {
-      sML[h] = mx;
-      sML[G + h] = ls;
-    }
-  }
-  __syncthreads();
-  // outputs (h, d) two per thread and pass, 8 records of each in flight,
-  // summed in record order
-  for (int ia = tid; ia < G * kDim; ia += 2 * kThreads) {
-    const int ib = ia + kThreads;
-    const bool two = ib < G * kDim;             // the same in a whole warp
-    const int ha = ia / kDim, da = ia % kDim;
-    const int hb = two ? ib / kDim : ha, db = two ? ib % kDim : da;
-    const float* pa = recs + (size_t)ha * S * (kDim + 2) + 2 + da;
-    const float* pb = recs + (size_t)hb * S * (kDim + 2) + 2 + db;
-    const float* wa = sw + ha * S;
-    const float* wb = sw + hb * S;
-    float aa = 0.f, ab = 0.f;
-    int s = 0;
-    for (; s + 8 <= S; s += 8) {
-      float xa[8], xb[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        xa[u] = __ldcg(pa + (size_t)(s + u) * (kDim + 2));
-        xb[u] = __ldcg(pb + (size_t)(s + u) * (kDim + 2));
+      for (int u = 0; u < kMergeBatch; ++u) {
+        const bool ok = s0 + u < S;
+        const float* r = rh + (size_t)(s0 + u) * (kDim + 2);
+        m[u] = ok ? __ldcg(r) : -INFINITY;
+        l[u] = ok ? __ldcg(r + 1) : 0.f;
+        xa[u] = ok ? __ldcg(r + 2 + d) : 0.f;
+        xb[u] = ok ? __ldcg(r + 2 + d + kHalf) : 0.f;
       }
+      float bm = mx;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        aa = fmaf(wa[s + u], xa[u], aa);
-        ab = fmaf(wb[s + u], xb[u], ab);
+      for (int u = 0; u < kMergeBatch; ++u) bm = fmaxf(bm, m[u]);
+      if (bm == -INFINITY) continue;            // every record so far is empty
+      const float a = (mx == -INFINITY) ? 0.f : ex2(mx - bm);
+      ls *= a;
+      oa *= a;
+      ob *= a;
+#pragma unroll
+      for (int u = 0; u < kMergeBatch; ++u) {
+        const float w = (m[u] == -INFINITY) ? 0.f : ex2(m[u] - bm);
+        ls = fmaf(w, l[u], ls);
+        oa = fmaf(w, xa[u], oa);
+        ob = fmaf(w, xb[u], ob);
       }
+      mx = bm;
     }
-    for (; s < S; ++s) {
-      aa = fmaf(wa[s], __ldcg(pa + (size_t)s * (kDim + 2)), aa);
-      ab = fmaf(wb[s], __ldcg(pb + (size_t)s * (kDim + 2)), ab);
-    }
-    const float La = sML[G + ha];
-    p.o[(size_t)(bh0 + ha) * kDim + da] = __float2bfloat16_rn(La > 0.f ? aa / La : 0.f);
-    if (two) {
-      const float Lb = sML[G + hb];
-      p.o[(size_t)(bh0 + hb) * kDim + db] = __float2bfloat16_rn(Lb > 0.f ? ab / Lb : 0.f);
-    }
-  }
-  if (tid < G && p.lse != nullptr) {
-    const float L = sML[G + tid];
-    p.lse[bh0 + tid] = (L > 0.f) ? (sML[tid] + lg2(L)) * kLn2 : -INFINITY;
+    __nv_bfloat16* out = p.o + (size_t)(bh0 + h) * kDim;
+    out[d] = __float2bfloat16_rn(ls > 0.f ? oa / ls : 0.f);
+    out[d + kHalf] = __float2bfloat16_rn(ls > 0.f ? ob / ls : 0.f);
+    if (d == 0 && p.lse != nullptr) p.lse[bh0 + h] = (ls > 0.f) ? (mx + lg2(ls)) * kLn2 : -INFINITY;
   }
   if (tid == 0) p.ws_count[bkv * n_slices + slice] = 0;  // leave the workspace zeroed for the next call
 }
@@ -650,12 +672,11 @@ inline long long n_slices(long long G) { return (G + kSliceHeads - 1) / kSliceHe
 
 // Split records one last CTA merges (heads x splits): more splits spread the
 // stream over more SMs, but the merge runs on one SM (256 measured best of
-// 64-1024 over G = 2-32, B = 1-8).
+// 64-1024 over G = 2-32, B = 1-8, with an earlier merge).
 constexpr long long kMaxRecords = 256;
 
 // One CTA per SM; chunks are whole tiles; at most kMaxRecords / (heads of a
-// slice) splits (the merge weights, heads x splits floats, fit in the idle
-// K/V ring).
+// slice) splits.
 inline Plan tc_plan(long long B, long long H, long long H_kv, long long n, int num_sms, bool ragged,
                     int ctas_per_sm = 1) {
   const long long G = H / H_kv;
@@ -677,16 +698,25 @@ int launch_np(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, d
   const int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(gqa_tc_kernel<T, KVT, NP>), smem,
                                       "grouped-head decode (tensor core) shared memory");
   if (rc) return rc;
-  gqa_tc_kernel<T, KVT, NP><<<grid, kThreads, smem, st>>>(tk, tv, prm);
-  return check_cuda(cudaGetLastError(), "grouped-head decode (tensor core) launch");
+  // programmatic stream serialization: the CTAs may take SMs as the previous
+  // kernel's CTAs leave (the kernel waits in grid_dep_wait before it touches
+  // global memory)
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, gqa_tc_kernel<T, KVT, NP>, tk, tv, prm),
+                    "grouped-head decode (tensor core) launch");
 }
 
 inline int launch(const Params& prm, int q_dtype, int kv_dtype, long long B, long long H_kv, cudaStream_t st) {
   const bool f8 = kv_dtype == PU_DTYPE_FP8_E4M3;
-  const long long ring = f8 ? (long long)Ring<__nv_fp8_e4m3>::NS * 2 * Ring<__nv_fp8_e4m3>::kTileBytes
-                            : (long long)Ring<__half>::NS * 2 * Ring<__half>::kTileBytes;
-  if ((long long)kSliceHeads * prm.splits + 2 * kSliceHeads > ring / 4)
-    return set_error(PU_ERR_UNSUPPORTED, "grouped-head decode: %d splits exceed the merge space", prm.splits);
   CUtensorMap tk, tv;
   int rc = f8 ? make_tmap_u8_3d(&tk, prm.k, kDim, prm.n_local, B * H_kv, kDim, BT, true)
               : make_tmap_bf16_3d(&tk, prm.k, kDim, prm.n_local, B * H_kv, 64, BT, true);

@@ -114,6 +114,21 @@ __device__ __forceinline__ bool bar_any_named(int id, int count, bool pred) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch (a kernel launched with programmatic stream
+// serialization may start while the previous kernel of its stream finishes)
+// ---------------------------------------------------------------------------
+// Blocks until every prerequisite grid has completed and its memory
+// operations are visible; returns at once when there is none.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the dependent grid be scheduled once every CTA of this grid has
+// executed this or exited (the dependent still waits in grid_dep_wait for
+// this grid's completion before it touches memory).
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
