@@ -162,64 +162,46 @@ struct KVIO<__nv_fp8_e4m3> {
 };
 
 // Merge the nrec split records {m (log2 units), l, o[D]} of one (b, h) with a
-// stable LogSumExp, using every thread of the block: the maximum and the
-// weights 2^(m_g - M) are computed one record per thread, then thread d < D
-// sums column d over the records in order, eight loads in flight (a loop that
-// waited for each record's load in turn would chain one L2 round trip per
-// record at the end of the kernel).  M and L reach every thread, O threads
-// d < D.  sm_w: kThreads floats, sm_red: kWarps floats of shared memory.
+// stable LogSumExp.  Thread d < D reads the records kMergeBatch at a time,
+// every load of a batch in flight together (one L2 round trip per batch, at
+// the end of the kernel where nothing hides it), and folds them in record
+// order into a running maximum M, sum L and column d's sum O; threads d >= D
+// return M = -inf, L = O = 0.  No barrier inside.
+constexpr int kMergeBatch = 16;
+
 template <int D>
-__device__ __forceinline__ void block_merge(const float* rec, int nrec, float* sm_w, float* sm_red, float& M,
-                                            float& L, float& O) {
+__device__ __forceinline__ void block_merge(const float* rec, int nrec, float& M, float& L, float& O) {
   constexpr int stride = D + 2;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  float mx = -INFINITY;
-  for (int g = t; g < nrec; g += kThreads) mx = fmaxf(mx, __ldcg(rec + (size_t)g * stride));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  if (lane == 0) sm_red[warp] = mx;
-  __syncthreads();
-  M = sm_red[0];
-#pragma unroll
-  for (int w = 1; w < kWarps; ++w) M = fmaxf(M, sm_red[w]);
-  __syncthreads();
+  const int d = threadIdx.x;
+  M = -INFINITY;
   L = 0.f;
   O = 0.f;
-  if (M == -INFINITY) return;  // every record empty (the same M in every thread)
-  float lsum = 0.f;
-  for (int c = 0; c < nrec; c += kThreads) {
-    const int g = c + t;
-    float w = 0.f;
-    if (g < nrec) {
-      const float* r = rec + (size_t)g * stride;
-      const float mg = __ldcg(r);
-      const float lg = __ldcg(r + 1);
-      w = (mg == -INFINITY) ? 0.f : ex2(mg - M);
-      lsum += w * lg;
-    }
-    sm_w[t] = w;
-    __syncthreads();
-    if (t < D) {
-      const int n = min(kThreads, nrec - c);
-      const float* base = rec + (size_t)c * stride + 2 + t;
-      int j = 0;
-      for (; j + 8 <= n; j += 8) {
-        float x[8];
+  if (d >= D) return;
+  for (int c = 0; c < nrec; c += kMergeBatch) {
+    float m[kMergeBatch], l[kMergeBatch], x[kMergeBatch];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) x[u] = __ldcg(base + (size_t)(j + u) * stride);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) O = fmaf(sm_w[j + u], x[u], O);
-      }
-      for (; j < n; ++j) O = fmaf(sm_w[j], __ldcg(base + (size_t)j * stride), O);
+    for (int u = 0; u < kMergeBatch; ++u) {
+      const bool ok = c + u < nrec;
+      const float* r = rec + (size_t)(c + u) * stride;
+      m[u] = ok ? __ldcg(r) : -INFINITY;
+      l[u] = ok ? __ldcg(r + 1) : 0.f;
+      x[u] = ok ? __ldcg(r + 2 + d) : 0.f;
     }
-    __syncthreads();
+    float bm = M;
+#pragma unroll
+    for (int u = 0; u < kMergeBatch; ++u) bm = fmaxf(bm, m[u]);
+    if (bm == -INFINITY) continue;              // every record so far is empty
+    const float a = (M == -INFINITY) ? 0.f : ex2(M - bm);
+    L *= a;
+    O *= a;
+#pragma unroll
+    for (int u = 0; u < kMergeBatch; ++u) {
+      const float w = (m[u] == -INFINITY) ? 0.f : ex2(m[u] - bm);
+      L = fmaf(w, l[u], L);
+      O = fmaf(w, x[u], O);
+    }
+    M = bm;
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
-  if (lane == 0) sm_red[warp] = lsum;
-  __syncthreads();
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) L += sm_red[w];
 }
 
 // Push-mode merge for one (b, h): wait (bounded) until the words of every
@@ -320,8 +302,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
   __shared__ float sm_m[NGROUP];
   __shared__ float sm_l[NGROUP];
   __shared__ float sm_o[NGROUP][D];
-  __shared__ float sm_w[kThreads];
-  __shared__ float sm_red[kWarps];
   __shared__ int sm_last;
 
   const int tid = threadIdx.x;
@@ -332,6 +312,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
   const int split = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / p.H;
+  // launched with programmatic stream serialization: the CTAs may start while
+  // the previous kernel of the stream finishes; nothing in global memory is
+  // touched before this wait
+  grid_dep_wait();
+  grid_dep_launch_dependents();
 
   int len = p.n_local;
   if (p.lens != nullptr) {
@@ -494,9 +479,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
       rec[1] = L;
     }
   }
-  __threadfence();
   __syncthreads();
   if (tid == 0) {
+    // the barrier orders every thread's record stores before this fence, so
+    // one device-scope fence publishes the CTA's record before its count
+    __threadfence();
     const int prev = atomicAdd(p.ws_count + bh, 1);
     sm_last = (prev == p.splits - 1);
   }
@@ -506,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) split_kv_kernel(const Pa
 
   // last CTA of this (b, h): merge every split record
   float M, L, O;
-  block_merge<D>(p.ws_rec + (size_t)bh * p.splits * (D + 2), p.splits, sm_w, sm_red, M, L, O);
+  block_merge<D>(p.ws_rec + (size_t)bh * p.splits * (D + 2), p.splits, M, L, O);
   if (tid < D) {
     if constexpr (kFinal) {
       const float out = (L > 0.f) ? O / L : 0.f;
@@ -612,21 +599,42 @@ inline size_t workspace_bytes_any(long long BH, long long n_local, long long D, 
                   make_plan(BH, n_local, D, num_sms, true).total_bytes);
 }
 
+// Launch with programmatic stream serialization: the kernel's CTAs may be
+// placed on SMs while the previous kernel of the stream finishes (the kernel
+// waits in grid_dep_wait before it touches global memory).
+template <typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <bool kFinal, bool kPaged, bool kPush, typename QT, int DD>
 int launch_kv(const Params& prm, int kv_dtype, dim3 grid, cudaStream_t st) {
+  cudaError_t e;
   if (kv_dtype == PU_DTYPE_F16) {
-    split_kv_kernel<QT, __half, DD, kFinal, kPaged, kPush><<<grid, kThreads, 0, st>>>(prm);
+    e = launch_pdl(split_kv_kernel<QT, __half, DD, kFinal, kPaged, kPush>, grid, dim3(kThreads), 0, st, prm);
   } else if (kv_dtype == PU_DTYPE_BF16) {
-    split_kv_kernel<QT, __nv_bfloat16, DD, kFinal, kPaged, kPush><<<grid, kThreads, 0, st>>>(prm);
+    e = launch_pdl(split_kv_kernel<QT, __nv_bfloat16, DD, kFinal, kPaged, kPush>, grid, dim3(kThreads), 0, st, prm);
   } else {
     // fp8 caches are read by the single-GPU final-output step
     if constexpr (kFinal && !kPaged && !kPush) {
-      split_kv_kernel<QT, __nv_fp8_e4m3, DD, kFinal, kPaged, kPush><<<grid, kThreads, 0, st>>>(prm);
+      e = launch_pdl(split_kv_kernel<QT, __nv_fp8_e4m3, DD, kFinal, kPaged, kPush>, grid, dim3(kThreads), 0, st,
+                     prm);
     } else {
       return set_error(PU_ERR_UNSUPPORTED, "fp8 caches: single-GPU dense decode only");
     }
   }
-  return check_cuda(cudaGetLastError(), "split-KV decode launch");
+  return check_cuda(e, "split-KV decode launch");
 }
 
 template <bool kFinal, bool kPaged = false, bool kPush = false>

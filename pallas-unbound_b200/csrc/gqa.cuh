@@ -43,8 +43,6 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_kernel(const Params p) {
   __shared__ float sm_m[NGROUP];
   __shared__ float sm_l[NGROUP];
   __shared__ float sm_o[NGROUP][D];
-  __shared__ float sm_w[kThreads];
-  __shared__ float sm_red[kWarps];
   __shared__ int sm_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -201,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_kernel(const Params p) {
   for (int g = 0; g < G; ++g) {
     const int bh = bh0 + g;
     float M, L, O;
-    block_merge<D>(p.ws_rec + (size_t)bh * p.splits * (D + 2), p.splits, sm_w, sm_red, M, L, O);
+    block_merge<D>(p.ws_rec + (size_t)bh * p.splits * (D + 2), p.splits, M, L, O);
     if (tid < D) {
       p.o[(size_t)bh * D + tid] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
       if (tid == 0 && p.lse != nullptr) p.lse[bh] = (L > 0.f) ? (M + lg2(L)) * kLn2 : -INFINITY;

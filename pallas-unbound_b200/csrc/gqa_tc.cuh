@@ -698,20 +698,7 @@ int launch_np(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, d
   const int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(gqa_tc_kernel<T, KVT, NP>), smem,
                                       "grouped-head decode (tensor core) shared memory");
   if (rc) return rc;
-  // programmatic stream serialization: the CTAs may take SMs as the previous
-  // kernel's CTAs leave (the kernel waits in grid_dep_wait before it touches
-  // global memory)
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, gqa_tc_kernel<T, KVT, NP>, tk, tv, prm),
+  return check_cuda(launch_pdl(gqa_tc_kernel<T, KVT, NP>, grid, dim3(kThreads), smem, st, tk, tv, prm),
                     "grouped-head decode (tensor core) launch");
 }
 
