@@ -16,6 +16,12 @@
 //       the staging area of the tile's owner rank (t mod G) over NVLink, then
 //       raises a flag there: the reduce-scatter's traffic leaves tile by tile
 //       while the tensor cores keep multiplying.
+//   outproj_gemm_pair_kernel  the same for T a multiple of 256 on CTA pairs
+//       (clusters of two): 256 x 256 tiles, one tcgen05.mma.cta_group::2
+//       product per K step with each CTA holding half of the O rows and half
+//       of the W columns, which cuts the operand traffic per output by a
+//       third; each CTA's epilogue handles its 128 x 256 half exactly as the
+//       single-CTA kernel handles a tile.
 //   reduce_bcast_kernel  each owner waits (bounded) for its tiles' G partials,
 //       sums them in fp32 in rank order, rounds to bf16 and stores the result
 //       tile into every rank's result area, raising a flag there.
@@ -39,6 +45,10 @@
 
 #include <cuda_bf16.h>
 
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+
 #include "pu_host.cuh"
 #include "pu_ptx.cuh"
 
@@ -59,6 +69,17 @@ constexpr int kSmemBytes = kOffBar + 8 * (2 * NS + 4) + 16;
 constexpr int kTileBytes = BM * BN * 2;   // one bf16 output tile (64 KB)
 constexpr int kChunksPerRow = BN * 2 / 16;
 constexpr int kMaxRanks = 8;
+// CTA-pair kernel (T a multiple of 256): 256 x 256 tiles, one M = 256 product
+// per K step over the pair; each CTA holds 128 rows of the O tile and 128
+// columns of the W tile per stage (32 KB), so a pair reads 2 MB of operands
+// per 256 x 256 tile where two single-CTA tiles read 3 MB.
+constexpr int kPairRows = 2 * BM;
+constexpr int kPairStages = 6;
+constexpr int kTileBHalf = BK * (BN / 2) * 2;
+constexpr int kPairStage = kTileA + kTileBHalf;
+constexpr int kPairOffBar = kPairStages * kPairStage;
+// barriers: full[S], empty[S], acc_full[2], acc_empty[2]
+constexpr int kPairSmemBytes = kPairOffBar + 8 * (2 * kPairStages + 4) + 16;
 
 struct Layout {
   int n_tiles, n_owned;
@@ -84,6 +105,7 @@ struct Params {
   int n_k;                         // K / BK
   int n_ntiles;                    // N / BN
   int n_tiles, n_owned;
+  int n_pair_tiles;                // (T / 256) * (N / 256) for the CTA-pair kernel
   size_t off_part, off_res, off_pflag, off_rflag;
   uint64_t timeout_ns;
   __nv_bfloat16* y;                // caller's output [T, N]
@@ -123,6 +145,52 @@ __device__ __forceinline__ bool wait_flag(const unsigned* f, unsigned epoch, uin
 }
 __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Epilogue of one 128 x 256 output tile `tile` (row-major tile index over
+// T/128 x N/256) held in TMEM columns [acc, acc + 256) of lanes 0-127: warp
+// quarter q = warp % 4 reads lanes 32q..32q+31 (thread = tile row r) and
+// stores the bf16 row into Y (one rank) or chunk-major into the tile owner's
+// partial slot (then raises the owner's flag once all 128 threads stored).
+// Called by the four epilogue warps (128 threads, named barrier 1).
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc, int tile, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int q = warp & 3;
+  const int r = q * 32 + lane;                      // tile row
+  const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+  const int owner = tile % p.G;
+  uint4* dst = reinterpret_cast<uint4*>(p.exch[owner] + part_off(p, p.rank, tile / p.G));
+  // one rank: nothing to reduce, the tile goes straight into Y (row-major)
+  uint4* ydst = reinterpret_cast<uint4*>(p.y + (size_t)((tile / p.n_ntiles) * BM + r) * p.N +
+                                         (tile % p.n_ntiles) * BN);
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t v[32];
+    tmem_ld32(tmem_acc + lane_base + c * 32, v);
+    tmem_wait_ld();
+    reg_fence(v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 w = make_uint4(pack_bf16x2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
+                                 pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
+                                 pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
+                                 pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
+      if (p.G == 1)
+        ydst[c * 4 + j] = w;
+      else
+        dst[(c * 4 + j) * BM + r] = w;              // chunk-major: a warp writes 512 bytes
+    }
+  }
+}
+
+__device__ __forceinline__ void epilogue_flag(const Params& p, int tile, int tid) {
+  if (p.G == 1) return;
+  named_bar(1, 128);
+  if (tid == 64) {
+    // the barrier orders the other threads' stores before this fence
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<unsigned*>(p.exch[tile % p.G] + pflag_off(p, p.rank, tile / p.G)), p.epoch);
+  }
 }
 
 // Persistent GEMM + bf16 partial tiles to their owner ranks.
@@ -211,9 +279,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // epilogue: warps 2-5; TMEM lane quarter = warp % 4
-    const int q = warp & 3;
-    const int r = q * 32 + lane;                      // tile row
-    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     int i = 0;
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++i) {
       const int a = i & 1;
@@ -221,38 +286,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int owner = tile % p.G;
-      uint4* dst = reinterpret_cast<uint4*>(p.exch[owner] + part_off(p, p.rank, tile / p.G));
-      // one rank: nothing to reduce, the tile goes straight into Y (row-major)
-      uint4* ydst = reinterpret_cast<uint4*>(p.y + (size_t)((tile / p.n_ntiles) * BM + r) * p.N +
-                                             (tile % p.n_ntiles) * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + a * BN + c * 32, v);
-        tmem_wait_ld();
-        reg_fence(v);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 w = make_uint4(pack_bf16x2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
-                                     pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
-                                     pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
-                                     pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
-          if (p.G == 1)
-            ydst[c * 4 + j] = w;
-          else
-            dst[(c * 4 + j) * BM + r] = w;            // chunk-major: a warp writes 512 bytes
-        }
-      }
+      epilogue_tile(p, tmem + a * BN, tile, tid);
       tc_fence_before();
       mbar_arrive(bAccEmpty + a);                     // TMEM accumulator a is free again
-      if (p.G == 1) continue;
-      named_bar(1, 128);
-      if (tid == 64) {
-        // the CTA barrier orders the other threads' stores before this fence
-        __threadfence_system();
-        st_release_sys(reinterpret_cast<unsigned*>(p.exch[owner] + pflag_off(p, p.rank, tile / p.G)), p.epoch);
-      }
+      epilogue_flag(p, tile, tid);
     }
   }
   tc_fence_before();
@@ -260,6 +297,150 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
+// The same GEMM over CTA pairs (clusters of two): the even CTA's thread
+// issues tcgen05.mma.cta_group::2 products of 256 x 256 x 16, A = the pair's
+// 256 O rows (128 in each CTA's shared memory), B = the tile's 256 W columns
+// (128 in each CTA's shared memory); each CTA's TMEM holds its 128 rows of
+// the fp32 accumulator (double-buffered, 2 x 256 columns).
+//   warp 0   TMA producer of each CTA: its O rows and W columns; the loads of
+//            both CTAs count on the even CTA's full barrier (armed by the
+//            even CTA for the bytes of both)
+//   warp 1   even CTA: the product issuer; it commits each stage's products to
+//            both CTAs' empty barriers and each tile's to both CTAs'
+//            accumulator barriers; both CTAs: TMEM allocation
+//   warps 2-5 epilogue of each CTA: its 128-row half of the tile (one of the
+//            128 x 256 tiles of the single-CTA kernel, so the exchange,
+//            reduction and receive steps are shared), then an arrival on the
+//            even CTA's accumulator-empty barrier
+// Every wait is bounded; both CTAs always reach the closing cluster barrier,
+// after which no CTA touches the other's shared memory.
+__global__ void __launch_bounds__(kThreads, 1)
+    outproj_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmW,
+                             const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (smem_u32(smem) & 1023u) {                     // the same in both CTAs of a pair
+    if (tid == 0) record_device_error(PU_ERR_UNSUPPORTED, kSiteOutProj);
+    return;
+  }
+  const uint32_t rank = cluster_ctarank();
+  const bool lead = rank == 0;
+  const int pair = (int)blockIdx.x >> 1, n_pairs = (int)gridDim.x >> 1;
+  uint64_t* bFull = reinterpret_cast<uint64_t*>(smem + kPairOffBar);
+  uint64_t* bEmpty = bFull + kPairStages;
+  uint64_t* bAccFull = bEmpty + kPairStages;  // [2] accumulator a complete
+  uint64_t* bAccEmpty = bAccFull + 2;         // [2] (even CTA) accumulator a read out by both epilogues
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bAccEmpty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if (tid == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(bFull + s, 1);
+      mbar_init(bEmpty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bAccFull + a, 1);
+      mbar_init(bAccEmpty + a, 8);                  // 4 epilogue warps x 2 CTAs
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();                                   // barriers of both CTAs initialised
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmO);
+      tma_prefetch_desc(&tmW);
+      int g = 0;                                    // stages loaded so far
+      bool ok = true;
+      for (int tile = pair; ok && tile < p.n_pair_tiles; tile += n_pairs) {
+        const int m0 = (tile / p.n_ntiles) * kPairRows + (int)rank * BM;
+        const int n0 = (tile % p.n_ntiles) * BN + (int)rank * (BN / 2);
+        for (int s = 0; s < p.n_k; ++s, ++g) {
+          const int st = g % kPairStages;
+          const uint32_t u = g / kPairStages;
+          if (u > 0 && !mbar_wait(bEmpty + st, (u - 1) & 1, abort_flag, kSiteOutProj)) { ok = false; break; }
+          uint8_t* sa = smem + st * kPairStage;
+          uint8_t* sb = sa + kTileA;
+          const uint32_t full_lead = mapa_shared(bFull + st, 0);
+          if (lead) mbar_arrive_expect_tx(bFull + st, 2 * kPairStage);
+          tma_load_3d_pair(sa, &tmO, full_lead, s * BK, m0, 0);
+          for (int b = 0; b < BN / 2 / 64; ++b)
+            tma_load_3d_pair(sb + b * (BK * 128), &tmW, full_lead, n0 + b * 64, s * BK, 0);
+        }
+      }
+      if (lead) {
+        // copies still in flight (the peer's included: they count on these
+        // barriers) land before the pair may exit
+        volatile int no_abort = 0;
+        for (int h = max(0, g - kPairStages); h < g; ++h)
+          mbar_wait(bFull + h % kPairStages, (h / kPairStages) & 1, &no_abort, kSiteOutProj);
+      }
+    }
+  } else if (warp == 1) {
+    if (lead && lane == 0) {
+      // A: O rows, K-major; B: W columns, MN-major (N contiguous), 64-column
+      // blocks of BK rows each LBO = BK * 128 bytes apart (two per CTA)
+      constexpr uint32_t idesc = make_idesc_bf16(kPairRows, BN, 0, 1);
+      int g = 0, i = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < p.n_pair_tiles; tile += n_pairs, ++i) {
+        const int a = i & 1;
+        if (i >= 2 && !mbar_wait(bAccEmpty + a, ((i >> 1) - 1) & 1, abort_flag, kSiteOutProj)) break;
+        tc_fence_after();
+        for (int s = 0; s < p.n_k; ++s, ++g) {
+          const int st = g % kPairStages;
+          if (!mbar_wait(bFull + st, (g / kPairStages) & 1, abort_flag, kSiteOutProj)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t da = make_sdesc_sw128(smem_u32(smem + st * kPairStage), 16, 1024);
+          const uint64_t db = make_sdesc_sw128(smem_u32(smem + st * kPairStage + kTileA), BK * 128, 1024);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_ss_pair(tmem + a * BN, sdesc_add(da, kk * 32), sdesc_add(db, kk * 16 * 128), idesc,
+                        (s > 0 || kk > 0));
+          mma_commit_pair(mapa_shared(bEmpty + st, 0));
+          mma_commit_pair(mapa_shared(bEmpty + st, 1));
+        }
+        if (ok) {
+          mma_commit_pair(mapa_shared(bAccFull + a, 0));
+          mma_commit_pair(mapa_shared(bAccFull + a, 1));
+        }
+      }
+    }
+  } else {
+    // epilogue: warps 2-5 of each CTA (TMEM lane quarter = warp % 4), its 128
+    // rows of the pair tile
+    int i = 0;
+    for (int tile = pair; tile < p.n_pair_tiles; tile += n_pairs, ++i) {
+      const int a = i & 1;
+      bool ok = mbar_wait(bAccFull + a, (i >> 1) & 1, abort_flag, kSiteOutProj);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      // this half is tile t of the single-CTA numbering (128 x 256 tiles)
+      const int t = ((tile / p.n_ntiles) * 2 + (int)rank) * p.n_ntiles + tile % p.n_ntiles;
+      epilogue_tile(p, tmem + a * BN, t, tid);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(bAccEmpty + a, 0));   // accumulator a read out here
+      epilogue_flag(p, t, tid);
+    }
+  }
+  tc_fence_before();
+  cluster_sync();                                   // no remote arrival or product is still pending
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 2 * BN);
   }
 }
 
@@ -356,6 +537,52 @@ __global__ void __launch_bounds__(256) receive_kernel(const Params p) {
   }
 }
 
+// The CTA-pair kernel serves T % 256 == 0 unless PU_OUTPROJ_PAIR=0 (the
+// single-CTA kernel then serves every shape; tests compare the two).
+inline bool pair_kernel_enabled() {
+  const char* e = getenv("PU_OUTPROJ_PAIR");
+  return !(e && e[0] == '0');
+}
+
+// One persistent pair per cluster slot the device can hold at once
+// (cudaOccupancyMaxActiveClusters, cached per device), so that no pair waits
+// for a second wave.
+inline int launch_pair(const CUtensorMap& tmO, const CUtensorMap& tmW, const Params& prm, cudaStream_t st) {
+  int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(outproj_gemm_pair_kernel), kPairSmemBytes,
+                                "outproj pair smem attribute");
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static std::mutex mu;
+  static int slots[64] = {0};
+  const int dev = current_device();
+  if (dev < 0) return PU_ERR_CUDA;
+  int n_slots = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    n_slots = dev < 64 ? slots[dev] : 0;
+    if (n_slots <= 0) {
+      cfg.gridDim = dim3(2 * (sm_count() / 2));
+      rc = check_cuda(cudaOccupancyMaxActiveClusters(&n_slots, outproj_gemm_pair_kernel, &cfg),
+                      "outproj pair occupancy");
+      if (rc) return rc;
+      if (n_slots <= 0) return set_error(PU_ERR_UNSUPPORTED, "no CTA pair of the out-projection fits an SM pair");
+      if (dev < 64) slots[dev] = n_slots;
+    }
+  }
+  cfg.gridDim = dim3(2 * std::min(prm.n_pair_tiles, n_slots));
+  return check_cuda(cudaLaunchKernelEx(&cfg, outproj_gemm_pair_kernel, tmO, tmW, prm), "outproj pair GEMM launch");
+}
+
 }  // namespace outproj
 }  // namespace pu
 
@@ -397,6 +624,7 @@ int pu_outproj_allreduce(const void* o_local, const void* w_local, void* y, void
   prm.n_ntiles = (int)(N / BN);
   prm.n_tiles = l.n_tiles;
   prm.n_owned = l.n_owned;
+  prm.n_pair_tiles = (int)((T / kPairRows) * (N / BN));
   prm.off_part = l.off_part;
   prm.off_res = l.off_res;
   prm.off_pflag = l.off_pflag;
@@ -410,11 +638,15 @@ int pu_outproj_allreduce(const void* o_local, const void* w_local, void* y, void
   rc = pu::make_tmap_bf16_3d(&tmW, w_local, (uint64_t)N, (uint64_t)K, 1, 64, BK, true);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = pu::set_max_dynamic_smem(reinterpret_cast<const void*>(outproj_gemm_kernel), kSmemBytes,
-                                "outproj smem attribute");
-  if (rc) return rc;
-  outproj_gemm_kernel<<<std::min(l.n_tiles, pu::sm_count()), kThreads, kSmemBytes, st>>>(tmO, tmW, prm);
-  rc = pu::check_cuda(cudaGetLastError(), "outproj GEMM launch");
+  if (T % kPairRows == 0 && pair_kernel_enabled()) {
+    rc = launch_pair(tmO, tmW, prm, st);
+  } else {
+    rc = pu::set_max_dynamic_smem(reinterpret_cast<const void*>(outproj_gemm_kernel), kSmemBytes,
+                                  "outproj smem attribute");
+    if (rc) return rc;
+    outproj_gemm_kernel<<<std::min(l.n_tiles, pu::sm_count()), kThreads, kSmemBytes, st>>>(tmO, tmW, prm);
+    rc = pu::check_cuda(cudaGetLastError(), "outproj GEMM launch");
+  }
   if (rc || G == 1) return rc;                        // one rank: the GEMM wrote y
   reduce_bcast_kernel<<<l.n_owned, 256, 0, st>>>(prm);
   rc = pu::check_cuda(cudaGetLastError(), "outproj reduce launch");

@@ -1,8 +1,10 @@
 """Output projection fused with the TP all-reduce (pu_outproj_allreduce) on
 one GPU (a one-rank group): the tcgen05 GEMM and the reduce / receive path
 against an fp32 product, over consecutive calls (both exchange slots), and
-the bounded wait of the reduction.  The two-GPU exchange is covered in
-test_gpu_multigpu.py.
+the bounded wait of the reduction.  T a multiple of 256 runs the CTA-pair
+kernel (cta_group::2, 256 x 256 tiles), other T the single-CTA kernel; both
+are checked against the fp32 product and against each other on the same
+inputs.  The two-GPU exchange is covered in test_gpu_multigpu.py.
 
 Tolerance: the result is the bf16 rounding of an fp32-accumulated product,
 so max |y - ref| <= 1e-2 * max |ref| and ||y - ref|| / ||ref|| <= 5e-3.
@@ -50,7 +52,8 @@ def _check(y, ref):
     assert err <= 1e-2 * ref.abs().max().item() and rel <= 5e-3, (err, rel)
 
 
-@pytest.mark.parametrize("T,K,N", [(128, 64, 256), (640, 192, 768), (2048, 2048, 2048)])
+@pytest.mark.parametrize("T,K,N", [(128, 64, 256), (640, 192, 768), (2048, 2048, 2048), (256, 64, 256),
+                                   (512, 192, 768), (1280, 1024, 512), (4096, 128, 2048)])
 def test_outproj_one_rank(group, T, K, N):
     from pallas_flash import _lib
     from pallas_flash.distributed.outproj import out_proj_all_reduce
@@ -61,6 +64,29 @@ def test_outproj_one_rank(group, T, K, N):
         torch.cuda.synchronize()
         _check(y, o.float() @ w.float())
     assert _lib.device_status() == (0, 0)
+
+
+@pytest.mark.parametrize("T,K,N", [(256, 64, 256), (768, 576, 1280), (16384, 2048, 2048)])
+def test_outproj_pair_matches_single(group, T, K, N, monkeypatch):
+    """The CTA-pair kernel against the single-CTA kernel on the same inputs:
+    both accumulate each output in fp32 over the same K steps of 16, so the
+    results agree to the last bf16 bit or nearly (|diff| <= 1 ulp of bf16
+    on at most 0.1 % of the outputs)."""
+    from pallas_flash import _lib
+    from pallas_flash.distributed.outproj import out_proj_all_reduce
+    o = _gen((T, K), 71)
+    w = _gen((K, N), 72, 1.0 / K ** 0.5)
+    y_pair = out_proj_all_reduce(o, w, group)
+    monkeypatch.setenv("PU_OUTPROJ_PAIR", "0")
+    y_single = out_proj_all_reduce(o, w, group)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == (0, 0)
+    d = (y_pair.float() - y_single.float()).abs()
+    ulp = y_single.float().abs().clamp_min(1e-30) * 2.0 ** -7
+    assert (d <= ulp).all(), d.max().item()
+    assert (d > 0).float().mean().item() <= 1e-3
+    if T * N <= (1 << 21):
+        _check(y_pair, o.float() @ w.float())
 
 
 def test_outproj_wait_runs_out(group):
