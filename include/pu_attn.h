@@ -414,7 +414,9 @@ PU_API int pu_decode_sharded(const void* q, int q_dtype,
  * partial tile into its owner's buffer over NVLink, the owners reduce and
  * broadcast, and every rank copies the result into y; each wait is bounded
  * by timeout_ns (<= 2 s): on expiry pu_device_status reports
- * PU_ERR_DEVICE_TIMEOUT, detail 401.
+ * PU_ERR_DEVICE_TIMEOUT, detail 401.  For T a multiple of 256 the GEMM runs
+ * on CTA pairs (clusters of two SMs, 256 x 256 tiles); the environment
+ * variable PU_OUTPROJ_PAIR=0 selects the single-CTA kernel for every T.
  */
 PU_API size_t pu_outproj_exchange_bytes(int64_t T, int64_t N, int64_t G);
 
