@@ -210,22 +210,6 @@ __device__ __forceinline__ void block_merge(const float* rec, int nrec, float& M
 // the block (d = thread index; threads d >= D only join the vote).  A wait
 // that runs out records PU_ERR_DEVICE_TIMEOUT (detail kSiteDecodePeer) and
 // the output is zeros.
-// Value of the 64-bit word at w once it carries `epoch`: x is a first read
-// of it (issued earlier, with the other words' reads in flight), re-read with
-// a bounded wait only while its epoch does not match.
-__device__ __forceinline__ bool ll_settle(const unsigned long long* w, unsigned long long x, unsigned epoch,
-                                          uint64_t timeout_ns, float& value) {
-  if ((unsigned)(x >> 32) != epoch) {
-    const uint64_t t0 = global_timer_ns();
-    do {
-      if (global_timer_ns() - t0 > timeout_ns) return false;
-      x = ld_volatile_u64(w);
-    } while ((unsigned)(x >> 32) != epoch);
-  }
-  value = __uint_as_float((unsigned)x);
-  return true;
-}
-
 template <int D>
 __device__ __forceinline__ void peer_merge(const unsigned long long* exch, int G, int BH, int bh, unsigned epoch,
                                            uint64_t timeout_ns, __nv_bfloat16* o, float* lse, int d) {
@@ -243,17 +227,41 @@ __device__ __forceinline__ void peer_merge(const unsigned long long* exch, int G
       wo[g] = ld_volatile_u64(r + 2 + d);
     }
   }
+  // Poll in rounds: every word whose epoch is not yet this call's is read
+  // again, all such reads of a round in flight together, so the wait ends one
+  // L2 round trip after the last rank's record lands (settling the words one
+  // at a time would chain up to three round trips per rank).
   bool ok = true;
+  if (d < D) {
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+      bool pending = false;
+#pragma unroll
+      for (int g = 0; g < kMaxPeers; ++g)
+        if (g < G)
+          pending |= ((unsigned)(wm[g] >> 32) != epoch) | ((unsigned)(wl[g] >> 32) != epoch) |
+                     ((unsigned)(wo[g] >> 32) != epoch);
+      if (!pending) break;
+      if (global_timer_ns() - t0 > timeout_ns) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int g = 0; g < kMaxPeers; ++g) {
+        if (g >= G) continue;
+        const unsigned long long* r = base + ((size_t)g * BH + bh) * (D + 2);
+        if ((unsigned)(wm[g] >> 32) != epoch) wm[g] = ld_volatile_u64(r);
+        if ((unsigned)(wl[g] >> 32) != epoch) wl[g] = ld_volatile_u64(r + 1);
+        if ((unsigned)(wo[g] >> 32) != epoch) wo[g] = ld_volatile_u64(r + 2 + d);
+      }
+    }
+  }
 #pragma unroll
   for (int g = 0; g < kMaxPeers; ++g) {
-    mg[g] = -INFINITY;
-    lg[g] = 0.f;
-    og[g] = 0.f;
-    if (d < D && g < G && ok) {
-      const unsigned long long* r = base + ((size_t)g * BH + bh) * (D + 2);
-      ok = ll_settle(r, wm[g], epoch, timeout_ns, mg[g]) && ll_settle(r + 1, wl[g], epoch, timeout_ns, lg[g]) &&
-           ll_settle(r + 2 + d, wo[g], epoch, timeout_ns, og[g]);
-    }
+    const bool have = ok && d < D && g < G;
+    mg[g] = have ? __uint_as_float((unsigned)wm[g]) : -INFINITY;
+    lg[g] = have ? __uint_as_float((unsigned)wl[g]) : 0.f;
+    og[g] = have ? __uint_as_float((unsigned)wo[g]) : 0.f;
   }
   if (!__syncthreads_and(ok)) {
     if (d == 0) record_device_error(PU_ERR_DEVICE_TIMEOUT, kSiteDecodePeer);
