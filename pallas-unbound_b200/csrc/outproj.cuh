@@ -24,9 +24,12 @@
 //       single-CTA kernel handles a tile.
 //   reduce_bcast_kernel  each owner waits (bounded) for its tiles' G partials,
 //       sums them in fp32 in rank order, rounds to bf16 and stores the result
-//       tile into every rank's result area, raising a flag there.
-//   receive_kernel       each rank waits (bounded) for every result tile and
-//       copies it into the caller's Y.
+//       tile into its own result area (local stores), raising its own flag.
+//   receive_kernel       each rank waits (bounded) for every result tile's
+//       flag in the owner's buffer and reads the tile from there (plain loads
+//       over NVLink for the other owners) into the caller's Y.  Pulling the
+//       results replaced owners storing every result tile into every rank's
+//       buffer: per-thread 16-byte stores to peer memory moved ~390 GB/s.
 // Every rank's Y is bitwise identical (each tile is reduced once, by its
 // owner).  Partials travel as bf16, as an all-reduce of bf16 data would.
 //
@@ -38,9 +41,12 @@
 //   partials [2][G][n_owned][128*256] bf16   slot (epoch & 1)
 //   results  [2][n_tiles][128*256] bf16
 //   flags    partial [2][G][n_owned] u32, result [2][n_tiles] u32 (epochs)
-// Double buffering by epoch parity is sufficient: a rank's call e+2 starts
-// after its receive of e+1, which needed every owner's reduce of e+1, which
-// each owner ran after its own receive of e (stream order).
+// Double buffering by epoch parity is sufficient.  Partials: a rank's call
+// e+2 starts after its receive of e+1, which needed every owner's reduce of
+// e+1, which each owner ran after its reduce of e (stream order).  Results:
+// an owner writes call e+2's results after every rank's partials of e+2
+// arrived, and each rank stores those only after its receive of e+1, so
+// after its receive of e.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -492,35 +498,36 @@ __global__ void __launch_bounds__(256) reduce_bcast_kernel(const Params p) {
     for (int u = 0; u < kU; ++u) {
       const uint4 out = make_uint4(pack_bf16x2(acc[u][0], acc[u][1]), pack_bf16x2(acc[u][2], acc[u][3]),
                                    pack_bf16x2(acc[u][4], acc[u][5]), pack_bf16x2(acc[u][6], acc[u][7]));
-      for (int g = 0; g < p.G; ++g)
-        *(reinterpret_cast<uint4*>(p.exch[g] + res_off(p, t)) + c0 + u * blockDim.x) = out;
+      *(reinterpret_cast<uint4*>(mine + res_off(p, t)) + c0 + u * blockDim.x) = out;
     }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    // the barrier orders the other threads' stores before this fence
     __threadfence_system();
-    for (int g = 0; g < p.G; ++g) st_release_sys(reinterpret_cast<unsigned*>(p.exch[g] + rflag_off(p, t)), p.epoch);
+    st_release_sys(reinterpret_cast<unsigned*>(mine + rflag_off(p, t)), p.epoch);
   }
 }
 
-// Every rank: wait for each result tile and copy it into Y, 32 rows at a
-// time through shared memory (chunk-major tile -> row-major Y, both sides
-// coalesced).
+// Every rank: wait for each result tile's flag in its owner's buffer, then
+// read the tile from the owner's memory (over NVLink for the other ranks'
+// tiles) and copy it into Y, 32 rows at a time through shared memory
+// (chunk-major tile -> row-major Y, both sides coalesced).
 __global__ void __launch_bounds__(256) receive_kernel(const Params p) {
   __shared__ int s_ok;
   __shared__ uint4 slab[32][kChunksPerRow + 1];      // +1: conflict-free transposed reads
-  const unsigned char* mine = p.exch[p.rank];
   const int tid = threadIdx.x;
   for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x) {
+    const unsigned char* owner = p.exch[t % p.G];
     if (tid == 0) {
-      s_ok = wait_flag(reinterpret_cast<const unsigned*>(mine + rflag_off(p, t)), p.epoch, p.timeout_ns);
+      s_ok = wait_flag(reinterpret_cast<const unsigned*>(owner + rflag_off(p, t)), p.epoch, p.timeout_ns);
       if (!s_ok) record_device_error(PU_ERR_DEVICE_TIMEOUT, kSiteOutProj);
     }
     __syncthreads();
     const bool ok = s_ok;
     if (!ok) return;
     const int m0 = (t / p.n_ntiles) * BM, n0 = (t % p.n_ntiles) * BN;
-    const uint4* src = reinterpret_cast<const uint4*>(mine + res_off(p, t));
+    const uint4* src = reinterpret_cast<const uint4*>(owner + res_off(p, t));
     for (int r0 = 0; r0 < BM; r0 += 32) {
       // chunk c of rows r0..r0+31 is 512 contiguous bytes
       for (int e = tid; e < 32 * kChunksPerRow; e += blockDim.x) {
