@@ -244,8 +244,9 @@ def single_rank_group():
     when there is nothing to exchange)."""
     import torch.distributed as dist
     if not dist.is_initialized():
-        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:" + str(_free_port()),
-                                rank=0, world_size=1)
+        import tempfile
+        store = os.path.join(tempfile.mkdtemp(prefix="pu_pg_"), "store")
+        dist.init_process_group("gloo", init_method="file://" + store, rank=0, world_size=1)
     return dist.group.WORLD
 
 
@@ -833,13 +834,6 @@ def bench_outproj(steps: int, warmup: int, rank: int, world: int):
         out[transport] = (us, lat, len(ring))
     del ring
     return out
-
-
-def _free_port() -> int:
-    import socket
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 def bench_gqa_decode(steps: int, warmup: int):

@@ -40,3 +40,12 @@ def assert_close_grad(actual, expected, rel=GRAD_REL, what="grad"):
     r = orc.compare(actual, expected)
     assert r["rel"] <= rel, f"{what}: {r}"
     return r
+
+
+def one_rank_init_method() -> str:
+    """Rendezvous URL for a one-rank process group: a store file in a fresh
+    temporary directory (no TCP port, so no collision with a port another
+    process is still holding)."""
+    import os
+    import tempfile
+    return "file://" + os.path.join(tempfile.mkdtemp(prefix="pu_pg_"), "store")

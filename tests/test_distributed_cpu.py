@@ -15,7 +15,6 @@ from __future__ import annotations
 
 import datetime
 import os
-import socket
 import sys
 from pathlib import Path
 
@@ -34,16 +33,15 @@ from oracle import attention as orc  # noqa: E402
 from pallas_flash.distributed import collectives, mesh  # noqa: E402
 
 
-def free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def rendezvous() -> str:
+    """Store-file URL for one multi-process group (no TCP port to collide
+    with one that another process still holds)."""
+    import tempfile
+    return "file://" + os.path.join(tempfile.mkdtemp(prefix="pu_pg_"), "store")
 
 
-def _init(rank, world, port, timeout_s=30):
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world,
+def _init(rank, world, url, timeout_s=30):
+    dist.init_process_group("gloo", init_method=url, rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=timeout_s))
 
 
@@ -99,7 +97,7 @@ def _decode_exchange(rank, world, port, result_path):
 @pytest.mark.parametrize("world", [2, 4])
 def test_sequence_sharded_decode_exchange(tmp_path, world):
     res = tmp_path / "res.txt"
-    mp.start_processes(_decode_exchange, args=(world, free_port(), str(res)), nprocs=world,
+    mp.start_processes(_decode_exchange, args=(world, rendezvous(), str(res)), nprocs=world,
                        start_method="spawn", join=True)
     assert res.read_text() == "ok"
 
@@ -122,7 +120,7 @@ def _leaver(rank, world, port, result_path):
 
 def test_lost_rank_is_detected_not_hung(tmp_path):
     res = tmp_path / "res.txt"
-    ctx = mp.start_processes(_leaver, args=(2, free_port(), str(res)), nprocs=2,
+    ctx = mp.start_processes(_leaver, args=(2, rendezvous(), str(res)), nprocs=2,
                              start_method="spawn", join=False)
     deadline = 90
     t0 = datetime.datetime.now()

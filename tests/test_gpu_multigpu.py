@@ -20,7 +20,6 @@ from __future__ import annotations
 
 import datetime
 import os
-import socket
 import sys
 from pathlib import Path
 
@@ -36,23 +35,17 @@ for p in (str(ROOT), str(ROOT / "pallas-unbound_b200"), str(ROOT / "tests")):
 pytestmark = pytest.mark.gpu
 
 
-def _port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, store, out_dir):
     import torch.distributed as dist
     from helpers import randn
     from oracle import attention as orc
     from pallas_flash.kernels.decoding import pallas_flash_decoding
     from pallas_flash.ops.interface import flash_attention_backward, flash_attention_forward
 
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world,
+    # the ranks meet through a store file (no TCP port to collide with one
+    # that another process still holds)
+    dist.init_process_group("nccl", init_method="file://" + store, rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     res = {}
@@ -152,7 +145,7 @@ def test_two_gpu_decode_and_partitioned_training(tmp_path, built_lib):
     import json
     import torch.multiprocessing as mp
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    mp.start_processes(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(2, str(tmp_path / "pg_store"), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
     for rank in range(2):
         res = json.loads(Path(tmp_path, f"rank{rank}.json").read_text())
         assert res["dec_o"]["max_abs"] <= 2e-2 and res["dec_o"]["rel"] <= 1e-2, res

@@ -5,7 +5,6 @@ test_gpu_multigpu.py."""
 from __future__ import annotations
 
 import datetime
-import socket
 
 import pytest
 import torch
@@ -18,12 +17,10 @@ def group(built_lib):
     if not torch.cuda.is_available():
         pytest.fail("CUDA device required for -m gpu tests")
     import torch.distributed as dist
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        port = s.getsockname()[1]
+    from helpers import one_rank_init_method
     already = dist.is_initialized()
     if not already:
-        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0,
+        dist.init_process_group("gloo", init_method=one_rank_init_method(), rank=0,
                                 world_size=1, timeout=datetime.timedelta(seconds=30))
     yield dist.group.WORLD
     from pallas_flash.distributed import peer
