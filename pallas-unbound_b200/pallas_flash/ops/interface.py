@@ -148,6 +148,17 @@ def _chunks(n: int, parts: int):
     return [(i * n // parts, (i + 1) * n // parts) for i in range(parts)]
 
 
+def _h2d(dst: torch.Tensor, src: torch.Tensor, D: int, dev: torch.device):
+    """Host rows `src` [n, N, D] into device rows `dst` [n, N, Dk] on the
+    current stream: one copy straight into `dst` when Dk == D and `src` is a
+    contiguous bf16 tensor, else through a device staging tensor (dtype cast,
+    or the first D of Dk columns)."""
+    if dst.shape[-1] == D and src.dtype == torch.bfloat16 and src.is_contiguous():
+        dst.copy_(src, non_blocking=True)
+    else:
+        dst[..., :D].copy_(src.to(dev, non_blocking=True))
+
+
 class _HostFlashAttention(torch.autograd.Function):
     """The attention of host tensors.  Heads are independent, so the B*H rows
     are processed in chunks on three streams: the host-to-device copy of chunk
@@ -166,9 +177,13 @@ class _HostFlashAttention(torch.autograd.Function):
         main = torch.cuda.current_stream(dev)
         s_in, s_out = _copy_streams(dev)
         hq, hk, hv = (t.detach().reshape(BH, t.shape[2], D) for t in (q, k, v))
-        q_ = torch.zeros((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
-        k_ = torch.zeros((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
-        v_ = torch.zeros((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
+        # unpadded head size: each chunk is copied straight into its slice
+        # (no zero fill, no staging tensor); padded: zero-filled, then the
+        # chunk lands in the first D columns
+        alloc = torch.empty if Dk == D else torch.zeros
+        q_ = alloc((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
+        k_ = alloc((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
+        v_ = alloc((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
         o = torch.empty((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
         lse = torch.empty((BH, Nq), dtype=torch.float32, device=dev)
         o_h = torch.empty((BH, Nq, D), dtype=torch.bfloat16, pin_memory=True)
@@ -177,7 +192,7 @@ class _HostFlashAttention(torch.autograd.Function):
         for a, b in _chunks(BH, _HOST_CHUNKS):
             with torch.cuda.stream(s_in):
                 for h, d in ((hq, q_), (hk, k_), (hv, v_)):
-                    d[a:b, :, :D].copy_(h[a:b].to(dev, non_blocking=True))
+                    _h2d(d[a:b], h[a:b], D, dev)
             main.wait_stream(s_in)
             flash_attention_forward(q_[a:b].unsqueeze(0), k_[a:b].unsqueeze(0), v_[a:b].unsqueeze(0),
                                     causal=causal, sm_scale=sm_scale, out=o[a:b].unsqueeze(0),
@@ -201,7 +216,7 @@ class _HostFlashAttention(torch.autograd.Function):
         main = torch.cuda.current_stream(dev)
         s_in, s_out = _copy_streams(dev)
         hdo = do.detach().reshape(BH, Nq, D)
-        do_ = torch.zeros((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
+        do_ = (torch.empty if Dk == D else torch.zeros)((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
         dq = torch.empty((BH, Nq, Dk), dtype=torch.bfloat16, device=dev)
         dk = torch.empty((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
         dv = torch.empty((BH, Nkv, Dk), dtype=torch.bfloat16, device=dev)
@@ -214,7 +229,7 @@ class _HostFlashAttention(torch.autograd.Function):
         s_in.wait_stream(main)
         for a, b in parts:
             with torch.cuda.stream(s_in):
-                do_[a:b, :, :D].copy_(hdo[a:b].to(dev, non_blocking=True))
+                _h2d(do_[a:b], hdo[a:b], D, dev)
             main.wait_stream(s_in)
             c = lambda t: t[a:b].unsqueeze(0)   # noqa: E731
             flash_attention_backward(c(q_), c(k_), c(v_), c(o), c(lse), c(do_), causal=ctx.causal,
